@@ -1,0 +1,386 @@
+#!/usr/bin/env python
+"""Benchmark: env plies/s for step + legal mask + 317-channel observation.
+
+One "step" is one ply over the whole batch: observation of every env's
+acting seat, a stand-in policy (uniform-random legal action, or a masked
+softmax over seeded N(0,1) logits), then the fused ply kernel (step, combat
+memory, beliefs, auto-reset from the setup pool, legal CSR + canonical mask
+of the new turn).  ``value`` counts plies actually applied (MoveResult
+valid) summed over ranks, divided by the max over ranks of the device time
+of the timed steps.  Inputs are device resident; every step writes
+>1.5 GB (observations), far above the 126 MB L2, so no flush is needed.
+
+``--impl reference`` times the CPU restatement of the reference rules (the
+oracle port; the reference itself is Python and does not travel to the GPU
+host) on the host cores, same metric and config, bounded sample.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+CONFIGS = {
+    # name: envs per GPU, observer seats per env, policy, pool size, plies, show mode
+    "cfg2": dict(envs=4096, seats=1, policy="uniform", pool=10_000, plies=1000, mode=2,
+                 workload="configs[1]: 4096 envs/GPU, step + CSR legal mask + 317-ch obs (acting seat), "
+                          "uniform-random legal policy, auto-reset from a seeded 10,000-setup pool"),
+    "cfg3": dict(envs=65536, seats=4, policy="softmax", pool=10_000, plies=100, mode=2,
+                 workload="configs[2]: 65536 envs, obs for all 4 seats, masked softmax over seeded N(0,1) logits"),
+    "cfg4": dict(envs=32768, seats=1, policy="softmax", pool=8192, plies=512, mode=2,
+                 workload="configs[3]: 32768 envs/GPU, 512-ply rollout, pool of 8192, masked softmax, "
+                          "episode stats all-reduced once per rollout"),
+}
+
+OBS_WRITE = 317 * 289 * 4 + 28 * 4  # bytes written per (env, seat) observation
+
+
+def obs_read_bytes() -> int:
+    """Bytes the observation kernel must read per (env, observer) unit."""
+    piece = 120 * (1 + 1 + 1 + 1 + 1 + 1 + 1 + 2 + 2 + 2 + 1 + 2 + 2)      # piece SoA fields read
+    cm_obs = 120 * (8 + 8 + 2 + 2 + 2 + 8 + 8 + 2 + 2 + 1 + 2 + 1 + 1 + 1)  # observer's CM row
+    cm_opp = 30 * 2 * (8 + 8 + 2 + 1 + 1) + 30 * 16                    # opponents' view of own pieces, eaten_by
+    other = 120 + 2 * 24 + 8 + 2 * 32 * 2 + 4 + 4 + 4                  # belief codes, remaining, flags, history
+    return piece + cm_obs + cm_opp + other
+
+
+def sample_clocks(dev: int, stop: threading.Event, rows: list) -> None:
+    q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+    try:
+        p = subprocess.Popen(["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits", "-i", str(dev),
+                              "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+    except OSError:
+        return
+    try:
+        while not stop.is_set():
+            line = p.stdout.readline()
+            if not line:
+                break
+            rows.append([x.strip() for x in line.split(",")])
+    finally:
+        p.terminate()
+        try:
+            p.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            p.kill()
+
+
+def summarize_clocks(rows: list) -> dict:
+    sm = [float(r[0]) for r in rows if len(r) >= 8 and r[0].replace(".", "").isdigit()]
+    mx = [float(r[1]) for r in rows if len(r) >= 8 and r[1].replace(".", "").isdigit()]
+    reasons = set()
+    for r in rows:
+        if len(r) < 8:
+            continue
+        for name, v in (("hw_slowdown", r[4]), ("hw_thermal_slowdown", r[5]), ("sw_thermal_slowdown", r[6]),
+                        ("sw_power_cap", r[7])):
+            if v.strip().lower() == "active":
+                reasons.add(name)
+    return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+            "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def peak_hbm() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return 6650.0, "fallback"
+
+
+def profiled_traffic(cfg: str) -> float | None:
+    """DRAM bytes per observation unit from the committed ncu summary, if any."""
+    p = ROOT / "profiles" / "obs_kernel_traffic.json"
+    if not p.exists():
+        return None
+    try:
+        d = json.loads(p.read_text())
+        return float(d["dram_bytes_per_unit"])
+    except Exception:
+        return None
+
+
+# ---------------------------------------------------------------------------
+# CPU arms (oracle = CPU restatement of the reference rules)
+# ---------------------------------------------------------------------------
+
+def cpu_rollout(envs: int, plies: int, seats: int, seed: int, threads: int, budget_s: float):
+    """Step + legal + observation on the CPU oracle; returns (plies/s, plies, seconds, sample text)."""
+    os.environ["JQ_ORACLE_THREADS"] = str(threads)
+    from junqi_b200 import tables
+    from oracle import oracle as O
+    pool = tables.build_setup_pool(256, seed=42)
+    b = O.OracleBatch(envs, 2)
+    b.threads = threads
+    rng = np.random.default_rng(seed)
+    for e in range(envs):
+        b.reset_env(e, pool[e % len(pool)])
+    done = 0
+    t0 = time.perf_counter()
+    t = 0
+    for t in range(plies):
+        if seats == 1:
+            b.obs()
+        else:
+            for s in range(4):
+                b.obs(np.full(envs, s, np.int8))
+        off, val = b.legal()
+        cnt = np.diff(off)
+        pick = (rng.random(envs) * np.maximum(cnt, 1)).astype(np.int64)
+        acts = np.where(cnt > 0, val[np.minimum(off[:-1] + pick, max(len(val) - 1, 0))] if len(val) else -1, -1)
+        r = b.step(acts.astype(np.int32))
+        done += int(r["valid"].sum())
+        for e in np.nonzero(r["terminated"])[0]:
+            b.reset_env(int(e), pool[int(rng.integers(len(pool)))])
+        if time.perf_counter() - t0 > budget_s:
+            break
+    dt = time.perf_counter() - t0
+    sample = f"{envs} envs x {t + 1} plies, step + legal + obs ({seats} seat/env), {threads} threads"
+    return done / dt, done, dt, sample
+
+
+def host_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def reference_arm(args, cfg: dict) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = host_cores()
+    from oracle import oracle as O
+    O.build()
+    envs = min(cfg["envs"], 256 * threads)
+    for _ in range(args.warmup if args.warmup < 3 else 2):
+        cpu_rollout(min(envs, 64), 1, cfg["seats"], args.seed, threads, 5.0)
+    rate, done, dt, sample = cpu_rollout(envs, args.steps, cfg["seats"], args.seed, threads, 120.0)
+    line = {"impl": "reference", "metric": "env plies/s (step + legal mask + 317-ch obs)", "value": rate,
+            "unit": "plies/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8/int16/f32",
+            "data": "synthetic (seeded setup pool, uniform-random legal policy)",
+            "config": {"workload": cfg["workload"], "envs_sampled": envs, "seats_per_env": cfg["seats"]},
+            "cpu_baseline": {"value": rate, "unit": "plies/s", "cores": threads, "kind": "port",
+                             "sample": sample + f", {dt:.1f} s"},
+            "e2e": {"value": rate, "unit": "plies/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=None, help="timed plies (default: the config's plies)")
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--config", default="cfg2", choices=sorted(CONFIGS))
+    ap.add_argument("--envs", type=int, default=None, help="envs per GPU (default: the config's)")
+    ap.add_argument("--e2e-steps", type=int, default=100)
+    ap.add_argument("--seed", type=int, default=2026)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    cfg = dict(CONFIGS[args.config])
+    if args.envs:
+        cfg["envs"] = args.envs
+    if args.steps is None:
+        args.steps = cfg["plies"]
+    if args.impl == "reference":
+        reference_arm(args, cfg)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+
+    from junqi_b200 import _native
+    from junqi_b200 import tables
+    from junqi_b200.env import JunqiEnvB200
+    _native.build()
+
+    n, seats = cfg["envs"], cfg["seats"]
+    seed = args.seed + rank * 10_000
+    pool = tables.build_setup_pool(cfg["pool"], seed=42)
+    env = JunqiEnvB200(n, device=local, show_mode=cfg["mode"], pool=pool, obs_seats=seats)
+    sampler = env.sample_uniform if cfg["policy"] == "uniform" else env.sample_softmax
+    env.reset(seed=seed)
+    stream = torch.cuda.current_stream()
+
+    def one_ply(t, ev=None):
+        if ev is not None:
+            ev[0].record(stream)
+        env.observe()
+        if ev is not None:
+            ev[1].record(stream)
+        acts = sampler(seed, t)
+        if ev is not None:
+            ev[2].record(stream)
+        env.ply(acts, seed=seed, ply=t)
+        if ev is not None:
+            ev[3].record(stream)
+        return env.out["valid"]
+
+    for t in range(1, args.warmup + 1):
+        one_ply(t)
+    env.stats.zero_()
+    applied = torch.zeros((), dtype=torch.int64, device=env.device)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clock_rows, stop = [], threading.Event()
+    th = threading.Thread(target=sample_clocks, args=(local, stop, clock_rows), daemon=True)
+    th.start()
+    time.sleep(0.5)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t_wall = time.perf_counter()
+    start.record(stream)
+    for k in range(args.steps):
+        t = args.warmup + 1 + k
+        applied += one_ply(t, evs[k]).sum(dtype=torch.int64)
+    if world > 1:
+        dist.all_reduce(env.stats)  # one collective per rollout: episode statistics
+    end.record(stream)
+    torch.cuda.synchronize()
+    t_wall = time.perf_counter() - t_wall
+    if world > 1:
+        dist.barrier()
+    stop.set()
+    th.join(timeout=10)
+    ms_total = start.elapsed_time(end)
+    obs_ms = [e[0].elapsed_time(e[1]) for e in evs]
+    ply_ms = [e[2].elapsed_time(e[3]) for e in evs]
+    plies_local = int(applied.item())
+    t_max = torch.tensor([ms_total], dtype=torch.float64, device=env.device)
+    tot = torch.tensor([plies_local], dtype=torch.int64, device=env.device)
+    if world > 1:
+        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
+        dist.all_reduce(tot)
+    ms_max = float(t_max.item())
+    plies_all = int(tot.item())
+    value = plies_all / (ms_max / 1e3)
+
+    # e2e through the public API with host buffers: H2D actions, D2H results + CSR, host policy
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(env, args, seed, stream)
+    stats = env.stats.cpu().numpy().tolist()
+
+    if rank == 0:
+        peak, peak_kind = peak_hbm()
+        units = n * seats
+        obs_bytes = units * (OBS_WRITE + obs_read_bytes())
+        obs_avg = statistics.mean(obs_ms)
+        achieved = obs_bytes / (obs_avg / 1e3) / 1e9
+        traffic_unit = profiled_traffic(args.config)
+        line = {
+            "metric": "env plies/s (step + legal mask + 317-ch obs)", "value": value, "unit": "plies/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8/int16/f32",
+            "data": "synthetic (seeded setup pool of random legal lineups, seeded policy)",
+            "config": {"workload": cfg["workload"], "envs_per_gpu": n, "seats_per_env": seats,
+                       "policy": cfg["policy"], "show_mode": "HALF_DARK", "plies_applied": plies_all,
+                       "l2": "per-step output (obs) > 1.5 GB >> 126 MB L2; no flush needed",
+                       "parallelism": f"env-sharded x{world} (weak)"},
+            "roofline": {"bound": "hbm", "kernel": "obs_kernel", "achieved": achieved, "peak": peak,
+                         "unit": "GB/s", "frac": achieved / peak, "peak_kind": peak_kind,
+                         "traffic": None if traffic_unit is None else traffic_unit * units,
+                         "algorithmic_bytes_per_launch": obs_bytes, "avg_launch_ms": obs_avg,
+                         "ply_kernel_avg_ms": statistics.mean(ply_ms)},
+            "clocks": summarize_clocks(clock_rows),
+            "gpu_launches": 3 * args.steps,
+            "episode_stats": {"wins_team0": stats[0], "wins_team1": stats[1], "draws": stats[2],
+                              "episodes": stats[3], "sum_len": stats[4]},
+            "wall_s": t_wall,
+        }
+        if e2e is not None:
+            line["e2e"] = e2e
+        if not args.no_cpu_baseline:
+            threads = host_cores()
+            rate, done, dt, sample = cpu_rollout(min(n, 64 * threads), 400, seats, args.seed, threads, 15.0)
+            line["cpu_baseline"] = {"value": rate, "unit": "plies/s", "cores": threads, "kind": "port",
+                                    "sample": sample + f", {dt:.1f} s"}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def run_e2e(env, args, seed, stream) -> dict:
+    """Same metric through the public API with host buffers every step."""
+    import torch
+    n = env.n
+    acts_h = torch.empty(n, dtype=torch.int32, pin_memory=True)
+    res_h = {k: torch.empty(n, dtype=v.dtype, pin_memory=True) for k, v in env.out.items()
+             if k in ("valid", "event", "terminated", "winner", "draw", "reward")}
+    off_h = torch.empty(n + 1, dtype=torch.int32, pin_memory=True)
+    val_h = torch.empty(n * env.cap, dtype=torch.int32, pin_memory=True)
+    acts_d = torch.empty(n, dtype=torch.int32, device=env.device)
+    rng = np.random.default_rng(seed)
+    env.legal()
+    off, val = env.csr()
+    off_h.copy_(off)
+    torch.cuda.synchronize()
+    tot = int(off_h[-1])
+    val_h[:tot].copy_(val[:tot])
+    applied, h2d, d2h = 0, 0, 0
+    steps = args.e2e_steps
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    start.record(stream)
+    for t in range(steps):
+        o = off_h.numpy()
+        cnt = np.diff(o)
+        pick = (rng.random(n) * np.maximum(cnt, 1)).astype(np.int64)
+        v = val_h.numpy()
+        acts_h.numpy()[:] = np.where(cnt > 0, v[np.minimum(o[:-1] + pick, max(int(o[-1]) - 1, 0))], -1)
+        acts_d.copy_(acts_h, non_blocking=True)
+        h2d += n * 4
+        env.ply(acts_d, seed=seed, ply=100_000 + t)
+        env.observe()
+        off, val = env.csr()
+        for k, h in res_h.items():
+            h.copy_(env.out[k], non_blocking=True)
+            d2h += h.numel() * h.element_size()
+        off_h.copy_(off, non_blocking=True)
+        torch.cuda.synchronize()
+        tot = int(off_h[-1])
+        val_h[:tot].copy_(val[:tot])
+        d2h += (n + 1) * 4 + tot * 4
+        applied += int(res_h["valid"].numpy().sum())
+    end.record(stream)
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end)
+    return {"value": applied / (ms / 1e3), "unit": "plies/s", "h2d_bytes_per_step": h2d // steps,
+            "d2h_bytes_per_step": d2h // steps, "steps": steps,
+            "api": "JunqiEnvB200.ply/observe/csr with pinned host actions in, MoveResult + CSR out"}
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,218 @@
+/*
+ * jq.h -- C ABI of the B200 JunQi environment library (libjq.so).
+ *
+ * One process drives one GPU.  All state lives in caller-owned device memory
+ * described by `jq_batch` (field-major SoA, one row per env); every entry
+ * point takes plain device pointers, sizes and a cudaStream_t (passed as
+ * void*), launches asynchronously on that stream and returns a status code.
+ * Nothing here synchronises the device or calls exit().
+ *
+ * Each entry point names the reference interface it replaces
+ * (freezeng123456/JunQi, src/env/cuda/src/bindings.cpp and
+ * src/env/cuda/include/junqi_cuda.h).
+ */
+#ifndef JQ_H
+#define JQ_H
+#include <stddef.h>
+#include <stdint.h>
+
+#define JQ_ABI_VERSION 1
+
+#define JQ_NUM_PIECES 120
+#define JQ_NUM_CELLS 289
+#define JQ_BOARD_SIZE 17
+#define JQ_NUM_SEATS 4
+#define JQ_NUM_OBS_CHANNELS 317
+#define JQ_NUM_GLOBAL_DIMS 28
+#define JQ_NUM_TRACKED_TYPES 12
+#define JQ_FLAT_ACTION_SPACE 16641 /* 129 x 129 compact canonical actions */
+#define JQ_HISTORY 32
+#define JQ_MAX_LEGAL 512
+#define JQ_RECENCY_LEN 4097
+
+/* Status codes. */
+enum {
+    JQ_OK = 0,
+    JQ_ERR_ARG = 1,       /* bad size / null pointer / out-of-range argument */
+    JQ_ERR_CUDA = 2,      /* a CUDA runtime call failed; see jq_last_error() */
+    JQ_ERR_NOT_READY = 3, /* jq_init / table uploads missing on this device */
+    JQ_ERR_CAPACITY = 4   /* an output buffer is too small */
+};
+
+/* Show modes (junqi_core/rules.py:598-603). */
+enum { JQ_BRIGHT = 0, JQ_DARK = 1, JQ_HALF_DARK = 2 };
+
+/*
+ * Batch of N envs.  Shapes are per env; every array is contiguous with the
+ * env index outermost.  Replaces DeviceGameStateBatch (junqi_cuda.h:48-111)
+ * plus the CombatMemory, move-history and belief buffers the reference keeps
+ * in process-global scratch.
+ */
+typedef struct jq_batch {
+    int32_t n;
+    uint8_t *alive;                    /* (120)  bool */
+    int8_t *piece_type, *piece_seat;   /* (120)  -1 for empty camp slots */
+    int8_t *pos_x, *pos_y;             /* (120)  -1 when dead */
+    int8_t *zero_x, *zero_y;           /* (120)  initial cell */
+    int16_t *move_count, *active_eat, *passive_surv; /* (120) */
+    int8_t *death_reason;              /* (120)  -1 alive */
+    int16_t *death_step, *death_loc;   /* (120)  -1 alive */
+    int16_t *cell_pid;                 /* (289)  -1 empty */
+    uint8_t *seat_dead, *seat_flag;    /* (4)    bool */
+    int8_t *turn;                      /* ()     */
+    int64_t *zobrist;                  /* ()     */
+    int32_t *move_counter, *mslc;      /* ()     */
+    uint8_t *terminated;               /* ()     bool */
+    int8_t *winner;                    /* ()     -1 none */
+    uint8_t *draw;                     /* ()     bool */
+    uint64_t *cm_direct_lo, *cm_direct_hi;      /* (4,120) */
+    uint16_t *cm_direct_type;                   /* (4,120) */
+    int16_t *cm_last_direct_step, *cm_direct_other; /* (4,120) */
+    uint64_t *cm_chain_lo, *cm_chain_hi;        /* (4,120) */
+    uint16_t *cm_chain_type;                    /* (4,120) */
+    int16_t *cm_last_chain_step;                /* (4,120) */
+    uint64_t *cm_eaten_lo, *cm_eaten_hi;        /* (4,120) */
+    int8_t *cm_rank_floor;                      /* (4,120) */
+    int16_t *cm_rank_floor_step;                /* (4,120) */
+    uint8_t *cm_is_gongb, *cm_not_gongb, *cm_atk_gongb; /* (4,120) bool */
+    int16_t *hist_src, *hist_dst;      /* (32)   ring of the last 32 moves */
+    int32_t *hist_count;               /* ()     moves recorded since reset */
+    uint8_t *bel_code;                 /* (4,120) per-observer belief code */
+    int16_t *remaining;                /* (4,4,12) per-observer enemy inventory */
+    uint8_t *rem_tracked;              /* (4,4)  bool */
+} jq_batch;
+
+/* Per-env step outputs (N each); any pointer may be NULL except valid. */
+typedef struct jq_step_out {
+    uint8_t *valid;
+    int8_t *event;
+    uint8_t *terminated;
+    int8_t *winner;
+    uint8_t *draw;
+    uint8_t *flag_captured;
+    float *reward;
+    int32_t *world_action;   /* filled by jq_step_canonical */
+} jq_step_out;
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+int jq_abi_version(void);
+const char *jq_last_error(void);
+
+/* Host-only dump of the board tables the kernels use, in flat cell space
+ * (no device needed): on-board / rail / curve-id / flag bits per cell, rail
+ * neighbours (289x4), straight rays (289x4x12), curve-chain rays (289x2x11),
+ * compact->flat (129).  Mirrors the junqi_core tables of
+ * _movegen_tables.py:130-470 and board.py:263-280 for parity tests. */
+int jq_topology_dump(int32_t *on_board, int32_t *rail, int32_t *curve, int32_t *rail_adj,
+                     int32_t *srays, int32_t *crays, int32_t *compact_to_flat, int32_t *flags);
+
+/* Make `device` current and build the board topology tables in constant
+ * memory.  Replaces init_tables / set_device (bindings.cpp:475-483,
+ * tables.cu:397-524). */
+int jq_init(int device);
+
+/* Upload the ten Zobrist tables (host pointers; shapes as in
+ * junqi_core/_zobrist.py:80-122).  Replaces upload_zobrist_tables
+ * (bindings.cpp:485-517). */
+int jq_upload_zobrist(const int64_t *piece /*120*14*289*/, const int64_t *turn /*4*/,
+                      const int64_t *move_counter /*4096*/, const int64_t *mslc /*512*/,
+                      const int64_t *winner /*3*/, int64_t terminated, int64_t draw,
+                      const int64_t *seat_dead /*4*/, const int64_t *seat_flag /*4*/,
+                      const int64_t *show_mode /*4*/);
+
+/* Upload observation tables (host pointers): per-slot belief prior (30x12),
+ * the uniform fallback vector (12) and the recency LUT (4 x 4097).
+ * Replaces upload_belief_prior_table (bindings.cpp:1234-1242). */
+int jq_upload_obs_tables(const float *prior /*30*12*/, const float *uniform12,
+                         const float *recency /*4*4097*/);
+
+/* Register the device-resident setup pool ((P,120) int8, piece type per
+ * pid, 0 on camp slots).  The pointer is kept until the next call.
+ * Replaces upload_setup_pool (bindings.cpp:1209-1222). */
+int jq_set_setup_pool(const int8_t *d_pool, int32_t pool_size);
+
+/* Pool index used by every reset: splitmix64(seed, ply, env) mod P. */
+int32_t jq_pool_index(uint64_t seed, uint64_t ply, int32_t env, int32_t pool_size);
+
+/* Reset every env whose terminated flag is set (or all envs when `all`)
+ * to GameState.new_game(pool[jq_pool_index(seed, ply, env)]) with fresh
+ * beliefs, zeroed combat memory and empty move history.  Replaces
+ * reset_terminated_envs + init_beliefs_for_reset_envs (bindings.cpp:1224-1262). */
+int jq_reset(const jq_batch *b, uint64_t seed, uint64_t ply, int32_t all, int32_t show_mode,
+             void *stream);
+
+/* Initial beliefs (BeliefTensor.initial for all four observers,
+ * info_model.py:218-270) and an empty move history for every env, for
+ * state written by the caller.  Replaces init_all_beliefs
+ * (bindings.cpp:1262-1270). */
+int jq_init_beliefs(const jq_batch *b, int32_t show_mode, void *stream);
+
+/* One ply for every env: world action id src_flat*289+dst_flat per env.
+ * BatchedGameState.step_batch semantics, plus combat memory, beliefs, move
+ * history and terminal reward.  Replaces DeviceGameStateBatch.step_batch /
+ * step_device (bindings.cpp:597-610, 1044-1074; game_state.cu:1307-1685). */
+int jq_step(const jq_batch *b, const int32_t *d_world_actions, int32_t show_mode,
+            const jq_step_out *out, void *stream);
+
+/* As jq_step, taking compact canonical actions (cs*129+cd) in each env's
+ * acting-seat frame; writes the world ids to out->world_action.
+ * Replaces step_device's rotate_actions_kernel path (game_state.cu:2639-2797). */
+int jq_step_canonical(const jq_batch *b, const int32_t *d_compact_actions,
+                      const int8_t *d_seats, int32_t show_mode, const jq_step_out *out,
+                      void *stream);
+
+/* Fused ply: jq_step, then auto-reset of the envs it terminated (pool
+ * index from (seed, ply, env)), then legal generation for the new turn
+ * (see jq_legal).  d_world_actions may be NULL to skip the step.  When
+ * d_stats is not NULL, each termination adds to d_stats[5] = {wins team 0,
+ * wins team 1, draws, episodes, sum of episode lengths in plies}. */
+int jq_ply(const jq_batch *b, const int32_t *d_world_actions, int32_t show_mode,
+           const jq_step_out *out, int32_t autoreset, uint64_t seed, uint64_t ply,
+           int32_t *d_counts, int32_t *d_ids, int32_t cap, uint8_t *d_mask,
+           int64_t *d_stats, void *stream);
+
+/* Legal actions for `d_seats` (NULL: each env's turn), ascending and
+ * de-duplicated per env (BatchedGameState.legal_action_ids_batch,
+ * batched_state.py:370-409).  Writes d_counts (N) and d_ids (N x cap);
+ * when d_mask is not NULL also the (N,16641) bool canonical mask in the
+ * seat's frame (game_state.cu:2291-2508, action_lut.py:174-212).
+ * Replaces legal_action_ids_batch / legal_mask_canonical_batch(_from_device). */
+int jq_legal(const jq_batch *b, const int8_t *d_seats, int32_t *d_counts, int32_t *d_ids,
+             int32_t cap, uint8_t *d_mask, void *stream);
+
+/* CSR from jq_legal's output: d_offsets (N+1) and d_values (sum counts).
+ * d_block_scratch must hold jq_csr_scratch_ints(N) int32.
+ * Replaces legal_action_ids_batch_csr (bindings.cpp:892-950). */
+int32_t jq_csr_scratch_ints(int32_t n);
+int jq_csr(int32_t n, const int32_t *d_counts, const int32_t *d_ids, int32_t cap,
+           int32_t *d_offsets, int32_t *d_values, int32_t *d_block_scratch, void *stream);
+
+/* 317-channel observation for `seats_per_env` observers per env:
+ * d_observers is (N, seats_per_env) int8 (NULL with seats_per_env==1 means
+ * each env's turn; NULL with 4 means seats 0..3).  Writes d_spatial
+ * (N*seats, 317, 17, 17) float32 and d_global (N*seats, 28) float32.
+ * ObservationBuilder._fill_into semantics (observation.py:598-858).
+ * Replaces build_observation_batch(_resident) / build_observation_single_seat
+ * (bindings.cpp:803-829, 1091-1182). */
+int jq_observe(const jq_batch *b, const int8_t *d_observers, int32_t seats_per_env,
+               int32_t show_mode, float *d_spatial, float *d_global, void *stream);
+
+/* Uniform-random legal action per env from jq_legal's output, counter-based
+ * (seed, ply, env); -1 when an env has no legal action. */
+int jq_sample_uniform(int32_t n, const int32_t *d_counts, const int32_t *d_ids, int32_t cap,
+                      uint64_t seed, uint64_t ply, int32_t *d_actions, void *stream);
+
+/* Masked-softmax sample over seeded N(0,1) logits on the compact canonical
+ * action space (Gumbel-max over the legal set).  Writes the compact
+ * canonical action (or -1) and its world id. */
+int jq_sample_softmax(const jq_batch *b, const int32_t *d_counts, const int32_t *d_ids,
+                      int32_t cap, uint64_t seed, uint64_t ply, int32_t *d_compact_actions,
+                      int32_t *d_world_actions, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,536 @@
+// jq_lib.cu -- kernels and the extern "C" entry points of libjq.so.
+//
+// Launch shapes: rules kernels run one warp per env with eight envs per CTA
+// and a grid sized to fill the device (grid-stride over envs), the board
+// tables staged once per CTA in shared memory; the observation kernel runs a
+// persistent grid of (SMs x resident CTAs) CTAs, one (env, observer) unit at a
+// time.  No entry point synchronises the device; every launch goes to the
+// caller's stream.
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "jq_obs.cuh"
+#include "jq_rules.cuh"
+#include "jq_topo_build.h"
+
+namespace jq {
+
+constexpr int RULE_WARPS = 8;
+constexpr int RULE_THREADS = RULE_WARPS * 32;
+
+enum : int { DO_STEP = 1, DO_RESET = 2, DO_LEGAL = 4, RESET_ALL = 8, DO_BELIEF_INIT = 16 };
+
+struct RuleSmem {
+    Topo topo;
+    WEnv w[RULE_WARPS];
+};
+
+struct RuleArgs {
+    jq_batch b;
+    const int32_t *acts;
+    int mode;
+    jq_step_out out;
+    uint64_t seed, ply;
+    const int8_t *pool;
+    int pool_size;
+    int32_t *counts, *ids;
+    int cap;
+    uint8_t *mask;
+    int64_t *stats;
+    const int8_t *seats;
+    int flags;
+};
+
+__device__ __forceinline__ int pool_index(uint64_t seed, uint64_t ply, int e, int P) {
+    return (int)(hash3(seed, ply, (uint64_t)e) % (uint64_t)P);
+}
+
+__global__ void __launch_bounds__(RULE_THREADS) rules_kernel(RuleArgs a) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    RuleSmem &S = *reinterpret_cast<RuleSmem *>(smem_raw);
+    {
+        const uint4 *src = reinterpret_cast<const uint4 *>(&c_topo);
+        uint4 *dst = reinterpret_cast<uint4 *>(&S.topo);
+        for (int k = threadIdx.x; k < (int)(sizeof(Topo) / 16); k += RULE_THREADS) dst[k] = src[k];
+        const unsigned char *s8 = reinterpret_cast<const unsigned char *>(&c_topo);
+        unsigned char *d8 = reinterpret_cast<unsigned char *>(&S.topo);
+        for (int k = (int)(sizeof(Topo) / 16) * 16 + threadIdx.x; k < (int)sizeof(Topo); k += RULE_THREADS)
+            d8[k] = s8[k];
+    }
+    __syncthreads();
+    const Topo &T = S.topo;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    WEnv &w = S.w[warp];
+    const jq_batch &b = a.b;
+    for (int e = blockIdx.x * RULE_WARPS + warp; e < b.n; e += gridDim.x * RULE_WARPS) {
+        warp_load(b, T, w, e, lane);
+        if (a.flags & DO_BELIEF_INIT) {
+            warp_belief_init(b, T, w, e, lane, a.mode);
+            b.hist_src[(size_t)e * HIST + lane] = -1;
+            b.hist_dst[(size_t)e * HIST + lane] = -1;
+            if (lane == 0) b.hist_count[e] = 0;
+            __syncwarp();
+        }
+        if (a.flags & DO_STEP) warp_step(b, T, w, e, lane, a.acts[e], a.mode, a.out, a.stats);
+        if (a.flags & DO_RESET) {
+            bool do_it = (a.flags & RESET_ALL) || b.terminated[e];
+            if (do_it && a.pool && a.pool_size > 0) {
+                const int8_t *lu = a.pool + (size_t)pool_index(a.seed, a.ply, e, a.pool_size) * NP;
+                warp_reset(b, T, w, e, lane, lu, a.mode);
+            }
+        }
+        __syncwarp();
+        if (a.flags & DO_LEGAL) {
+            int seat = a.seats ? a.seats[e] : b.turn[e];
+            bool skip = seat < 0 || seat > 3 || b.terminated[e] || w.sdead[seat & 3];
+            seat &= 3;
+            int cnt = warp_legal(T, w, lane, seat, skip, a.ids ? a.ids + (size_t)e * a.cap : nullptr, a.cap,
+                                 a.mask ? a.mask + (size_t)e * MASK_BYTES : nullptr);
+            if (lane == 0 && a.counts) a.counts[e] = cnt;
+        }
+        __syncwarp();
+    }
+}
+
+// compact canonical action -> world flat action (game_state.cu:2639-2685 semantics)
+__global__ void rotate_actions_kernel(int n, const int32_t *can, const int8_t *seats, const int8_t *turn,
+                                      int32_t *world) {
+    int e = blockIdx.x * blockDim.x + threadIdx.x;
+    if (e >= n) return;
+    int a = can[e];
+    int seat = (seats ? seats[e] : turn[e]) & 3;
+    if (a < 0 || a >= NB * NB) { world[e] = -1; return; }
+    int cs = a / NB, cd = a % NB;
+    // canonical -> world: invert the per-seat rotation by search over the 129 cells
+    int ws = -1, wd = -1;
+    for (int c = 0; c < NB; ++c) {
+        int r = c_topo.rot[seat][c];
+        if (r == cs) ws = c;
+        if (r == cd) wd = c;
+    }
+    world[e] = (ws < 0 || wd < 0) ? -1 : c_topo.c2f[ws] * NC + c_topo.c2f[wd];
+}
+
+// ---------------------------------------------------------------------------
+// CSR: block sums, then per-block exclusive scan + value compaction
+// ---------------------------------------------------------------------------
+constexpr int CSR_BLOCK = 1024;
+
+__global__ void csr_partial_kernel(int n, const int32_t *counts, int cap, int32_t *partial) {
+    __shared__ int32_t red[32];
+    int e = blockIdx.x * CSR_BLOCK + threadIdx.x;
+    int v = e < n ? min(counts[e], cap) : 0;
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(FULL, v, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        int s = red[threadIdx.x];
+        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(FULL, s, o);
+        if (threadIdx.x == 0) partial[blockIdx.x] = s;
+    }
+}
+
+__global__ void csr_finalize_kernel(int n, const int32_t *counts, const int32_t *ids, int cap,
+                                    const int32_t *partial, int32_t *offsets, int32_t *values) {
+    __shared__ int32_t wsum[32];
+    __shared__ int32_t base_s;
+    __shared__ int32_t offs[CSR_BLOCK];
+    if (threadIdx.x == 0) {
+        int s = 0;
+        for (int k = 0; k < (int)blockIdx.x; ++k) s += partial[k];
+        base_s = s;
+    }
+    int e = blockIdx.x * CSR_BLOCK + threadIdx.x;
+    int v = e < n ? min(counts[e], cap) : 0;
+    int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, inc = v;
+    for (int o = 1; o < 32; o <<= 1) {
+        int t = __shfl_up_sync(FULL, inc, o);
+        if (lane >= o) inc += t;
+    }
+    if (lane == 31) wsum[wid] = inc;
+    __syncthreads();
+    if (wid == 0) {
+        int s = wsum[lane], si = s;
+        for (int o = 1; o < 32; o <<= 1) {
+            int t = __shfl_up_sync(FULL, si, o);
+            if (lane >= o) si += t;
+        }
+        wsum[lane] = si - s;
+    }
+    __syncthreads();
+    int excl = base_s + wsum[wid] + inc - v;
+    offs[threadIdx.x] = excl;
+    if (e < n) offsets[e] = excl;
+    if (e == n - 1) offsets[n] = excl + v;
+    __syncthreads();
+    // one warp per env copies its ids
+    for (int k = wid; k < CSR_BLOCK; k += 32) {
+        int ee = blockIdx.x * CSR_BLOCK + k;
+        if (ee >= n) break;
+        int c = min(counts[ee], cap), o = offs[k];
+        for (int j = lane; j < c; j += 32) values[o + j] = ids[(size_t)ee * cap + j];
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Samplers (stand-in policies for benchmarks)
+// ---------------------------------------------------------------------------
+__global__ void sample_uniform_kernel(int n, const int32_t *counts, const int32_t *ids, int cap, uint64_t seed,
+                                      uint64_t ply, int32_t *acts) {
+    int e = blockIdx.x * blockDim.x + threadIdx.x;
+    if (e >= n) return;
+    int c = min(counts[e], cap);
+    acts[e] = c > 0 ? ids[(size_t)e * cap + (int)(hash3(seed, ply, (uint64_t)e) % (uint64_t)c)] : -1;
+}
+
+__device__ __forceinline__ float u01(uint64_t h) {  // (0, 1)
+    return ((float)(h >> 40) + 0.5f) * (1.0f / 16777216.0f);
+}
+
+// Gumbel-max over the legal set: argmax_a logit(a) + G(a), logit ~ N(0,1)
+// (Box-Muller) and G ~ Gumbel(0,1), both keyed on (seed, ply, env, action).
+__global__ void sample_softmax_kernel(int n, const int8_t *turn, const int32_t *counts, const int32_t *ids, int cap,
+                                      uint64_t seed, uint64_t ply, int32_t *can_out, int32_t *world_out) {
+    int e = blockIdx.x * blockDim.x + threadIdx.x;
+    if (e >= n) return;
+    int c = min(counts[e], cap), seat = turn[e] & 3;
+    float best = -3.0e38f;
+    int best_w = -1, best_c = -1;
+    for (int j = 0; j < c; ++j) {
+        int id = ids[(size_t)e * cap + j];
+        int sc = c_topo.f2c[id / NC], dc = c_topo.f2c[id % NC];
+        if (sc < 0 || dc < 0) continue;
+        int can = c_topo.rot[seat][sc] * NB + c_topo.rot[seat][dc];
+        uint64_t h = hash3(seed ^ 0xA5A5A5A5ull, ply, ((uint64_t)e << 16) ^ (uint64_t)can);
+        float r1 = u01(h), r2 = u01(mix64(h)), r3 = u01(mix64(h ^ 0x5bd1e995ull));
+        float logit = sqrtf(-2.f * logf(r1)) * cosf(6.2831853f * r2);
+        float score = logit - logf(-logf(r3));
+        if (score > best) { best = score; best_w = id; best_c = can; }
+    }
+    if (can_out) can_out[e] = best_c;
+    if (world_out) world_out[e] = best_w;
+}
+
+// ---------------------------------------------------------------------------
+// Host-side state
+// ---------------------------------------------------------------------------
+struct DeviceState {
+    bool topo = false, zob = false, obs = false;
+    const int8_t *pool = nullptr;
+    int pool_size = 0;
+    int sms = 0, rule_blocks_per_sm = 0, obs_blocks_per_sm = 0;
+};
+constexpr int MAX_DEV = 64;
+static DeviceState g_dev[MAX_DEV];
+static std::mutex g_mu;
+static thread_local char g_err[512] = "";
+
+static int fail(int code, const char *msg) {
+    std::snprintf(g_err, sizeof g_err, "%s", msg);
+    return code;
+}
+static int cuda_fail(cudaError_t err, const char *where) {
+    std::snprintf(g_err, sizeof g_err, "%s: %s", where, cudaGetErrorString(err));
+    return JQ_ERR_CUDA;
+}
+#define CU(call)                                                    \
+    do {                                                            \
+        cudaError_t _e = (call);                                    \
+        if (_e != cudaSuccess) return cuda_fail(_e, #call);         \
+    } while (0)
+
+static int current_dev(DeviceState *&st) {
+    int d = 0;
+    CU(cudaGetDevice(&d));
+    if (d < 0 || d >= MAX_DEV) return fail(JQ_ERR_ARG, "device index out of range");
+    st = &g_dev[d];
+    return JQ_OK;
+}
+
+static int check_batch(const jq_batch *b) {
+    if (!b || b->n <= 0) return fail(JQ_ERR_ARG, "batch is null or empty");
+    const void *ptrs[] = {b->alive, b->piece_type, b->piece_seat, b->pos_x, b->pos_y, b->zero_x, b->zero_y,
+                          b->move_count, b->active_eat, b->passive_surv, b->death_reason, b->death_step,
+                          b->death_loc, b->cell_pid, b->seat_dead, b->seat_flag, b->turn, b->zobrist,
+                          b->move_counter, b->mslc, b->terminated, b->winner, b->draw, b->cm_direct_lo,
+                          b->cm_direct_hi, b->cm_direct_type, b->cm_last_direct_step, b->cm_direct_other,
+                          b->cm_chain_lo, b->cm_chain_hi, b->cm_chain_type, b->cm_last_chain_step,
+                          b->cm_eaten_lo, b->cm_eaten_hi, b->cm_rank_floor, b->cm_rank_floor_step,
+                          b->cm_is_gongb, b->cm_not_gongb, b->cm_atk_gongb, b->hist_src, b->hist_dst,
+                          b->hist_count, b->bel_code, b->remaining, b->rem_tracked};
+    for (const void *p : ptrs)
+        if (!p) return fail(JQ_ERR_ARG, "a batch field pointer is null");
+    return JQ_OK;
+}
+
+static size_t rule_smem() { return sizeof(RuleSmem); }
+static size_t obs_smem() { return sizeof(ObsSmem); }
+
+static int launch_rules(RuleArgs &a, cudaStream_t s) {
+    DeviceState *st;
+    int rc = current_dev(st);
+    if (rc) return rc;
+    if (!st->topo) return fail(JQ_ERR_NOT_READY, "jq_init was not called on this device");
+    int blocks = (a.b.n + RULE_WARPS - 1) / RULE_WARPS;
+    int cap_blocks = st->sms * (st->rule_blocks_per_sm > 0 ? st->rule_blocks_per_sm : 1) * 4;
+    if (blocks > cap_blocks) blocks = cap_blocks;
+    rules_kernel<<<blocks, RULE_THREADS, rule_smem(), s>>>(a);
+    CU(cudaGetLastError());
+    return JQ_OK;
+}
+
+}  // namespace jq
+
+using namespace jq;
+
+extern "C" {
+
+int jq_abi_version(void) { return JQ_ABI_VERSION; }
+
+int jq_topology_dump(int32_t *on_board, int32_t *rail, int32_t *curve, int32_t *rail_adj, int32_t *srays,
+                     int32_t *crays, int32_t *compact_to_flat, int32_t *flags) {
+    static Topo T;
+    build_topo(T);
+    auto flat = [&](int c) { return c == NONE8 ? -1 : (int)T.c2f[c]; };
+    for (int f = 0; f < NC; ++f) {
+        int c = T.f2c[f];
+        on_board[f] = c >= 0;
+        rail[f] = c >= 0 && (T.flags[c] & F_RAIL) ? 1 : 0;
+        curve[f] = c >= 0 ? T.curve[c] : 0;
+        flags[f] = c >= 0 ? T.flags[c] : 0;
+        int n = 0;
+        for (int k = 0; k < 4; ++k) rail_adj[f * 4 + k] = -1;
+        if (c >= 0)
+            for (int v = 0; v < NB; ++v)
+                if ((T.railnb[c][v >> 5] >> (v & 31)) & 1u) rail_adj[f * 4 + n++] = T.c2f[v];
+        for (int k = 0; k < 4; ++k)
+            for (int l = 0; l < 12; ++l) srays[(f * 4 + k) * 12 + l] = c >= 0 ? flat(T.sray[c][k][l]) : -1;
+        for (int k = 0; k < 2; ++k)
+            for (int l = 0; l < 11; ++l) crays[(f * 2 + k) * 11 + l] = c >= 0 ? flat(T.cray[c][k][l]) : -1;
+    }
+    for (int c = 0; c < NB; ++c) compact_to_flat[c] = T.c2f[c];
+    return JQ_OK;
+}
+const char *jq_last_error(void) { return g_err; }
+
+int jq_init(int device) {
+    if (device < 0 || device >= MAX_DEV) return fail(JQ_ERR_ARG, "device index out of range");
+    CU(cudaSetDevice(device));
+    std::lock_guard<std::mutex> lk(g_mu);
+    DeviceState &st = g_dev[device];
+    if (st.topo) return JQ_OK;
+    static Topo host_topo;
+    static bool built = false;
+    if (!built) { build_topo(host_topo); built = true; }
+    CU(cudaMemcpyToSymbol(c_topo, &host_topo, sizeof(Topo)));
+    CU(cudaFuncSetAttribute(rules_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rule_smem()));
+    CU(cudaFuncSetAttribute(obs_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)obs_smem()));
+    CU(cudaDeviceGetAttribute(&st.sms, cudaDevAttrMultiProcessorCount, device));
+    CU(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&st.rule_blocks_per_sm, rules_kernel, RULE_THREADS, rule_smem()));
+    CU(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&st.obs_blocks_per_sm, obs_kernel, OBS_THREADS, obs_smem()));
+    st.topo = true;
+    return JQ_OK;
+}
+
+int jq_upload_zobrist(const int64_t *piece, const int64_t *turn, const int64_t *mc, const int64_t *mslc,
+                      const int64_t *winner, int64_t terminated, int64_t draw, const int64_t *seat_dead,
+                      const int64_t *seat_flag, const int64_t *show_mode) {
+    if (!piece || !turn || !mc || !mslc || !winner || !seat_dead || !seat_flag || !show_mode)
+        return fail(JQ_ERR_ARG, "null Zobrist table");
+    DeviceState *st;
+    int rc = current_dev(st);
+    if (rc) return rc;
+    CU(cudaMemcpyToSymbol(g_zpiece, piece, sizeof(int64_t) * NP * 14 * NC));
+    CU(cudaMemcpyToSymbol(g_zmc, mc, sizeof(int64_t) * 4096));
+    CU(cudaMemcpyToSymbol(g_zmslc, mslc, sizeof(int64_t) * 512));
+    CU(cudaMemcpyToSymbol(c_zturn, turn, sizeof(int64_t) * 4));
+    CU(cudaMemcpyToSymbol(c_zwin, winner, sizeof(int64_t) * 3));
+    CU(cudaMemcpyToSymbol(c_zsdead, seat_dead, sizeof(int64_t) * 4));
+    CU(cudaMemcpyToSymbol(c_zsflag, seat_flag, sizeof(int64_t) * 4));
+    CU(cudaMemcpyToSymbol(c_zshow, show_mode, sizeof(int64_t) * 4));
+    CU(cudaMemcpyToSymbol(c_zterm, &terminated, sizeof(int64_t)));
+    CU(cudaMemcpyToSymbol(c_zdraw, &draw, sizeof(int64_t)));
+    st->zob = true;
+    return JQ_OK;
+}
+
+int jq_upload_obs_tables(const float *prior, const float *uniform12, const float *recency) {
+    if (!prior || !uniform12 || !recency) return fail(JQ_ERR_ARG, "null observation table");
+    DeviceState *st;
+    int rc = current_dev(st);
+    if (rc) return rc;
+    CU(cudaMemcpyToSymbol(g_prior, prior, sizeof(float) * 360));
+    CU(cudaMemcpyToSymbol(g_uniform, uniform12, sizeof(float) * 12));
+    CU(cudaMemcpyToSymbol(g_recency, recency, sizeof(float) * 4 * RECENCY_LEN));
+    st->obs = true;
+    return JQ_OK;
+}
+
+int jq_set_setup_pool(const int8_t *d_pool, int32_t pool_size) {
+    if (!d_pool || pool_size <= 0) return fail(JQ_ERR_ARG, "empty setup pool");
+    DeviceState *st;
+    int rc = current_dev(st);
+    if (rc) return rc;
+    st->pool = d_pool;
+    st->pool_size = pool_size;
+    return JQ_OK;
+}
+
+int32_t jq_pool_index(uint64_t seed, uint64_t ply, int32_t env, int32_t pool_size) {
+    if (pool_size <= 0) return -1;
+    return (int32_t)(hash3(seed, ply, (uint64_t)env) % (uint64_t)pool_size);
+}
+
+static int rules_common(RuleArgs &a, const jq_batch *b, int mode, bool need_zob, void *stream) {
+    int rc = check_batch(b);
+    if (rc) return rc;
+    if (mode < 0 || mode > 2) return fail(JQ_ERR_ARG, "show_mode must be 0, 1 or 2");
+    DeviceState *st;
+    rc = current_dev(st);
+    if (rc) return rc;
+    if (need_zob && !st->zob) return fail(JQ_ERR_NOT_READY, "Zobrist tables not uploaded");
+    std::memset(&a, 0, sizeof a);
+    a.b = *b;
+    a.mode = mode;
+    a.pool = st->pool;
+    a.pool_size = st->pool_size;
+    (void)stream;
+    return JQ_OK;
+}
+
+int jq_reset(const jq_batch *b, uint64_t seed, uint64_t ply, int32_t all, int32_t show_mode, void *stream) {
+    RuleArgs a;
+    int rc = rules_common(a, b, show_mode, true, stream);
+    if (rc) return rc;
+    if (!a.pool) return fail(JQ_ERR_NOT_READY, "setup pool not set");
+    a.flags = DO_RESET | (all ? RESET_ALL : 0);
+    a.seed = seed;
+    a.ply = ply;
+    return launch_rules(a, (cudaStream_t)stream);
+}
+
+int jq_init_beliefs(const jq_batch *b, int32_t show_mode, void *stream) {
+    RuleArgs a;
+    int rc = rules_common(a, b, show_mode, false, stream);
+    if (rc) return rc;
+    a.flags = DO_BELIEF_INIT;
+    return launch_rules(a, (cudaStream_t)stream);
+}
+
+int jq_step(const jq_batch *b, const int32_t *d_world_actions, int32_t show_mode, const jq_step_out *out,
+            void *stream) {
+    RuleArgs a;
+    int rc = rules_common(a, b, show_mode, true, stream);
+    if (rc) return rc;
+    if (!d_world_actions || !out || !out->valid) return fail(JQ_ERR_ARG, "actions / outputs missing");
+    a.acts = d_world_actions;
+    a.out = *out;
+    a.flags = DO_STEP;
+    return launch_rules(a, (cudaStream_t)stream);
+}
+
+int jq_step_canonical(const jq_batch *b, const int32_t *d_compact_actions, const int8_t *d_seats,
+                      int32_t show_mode, const jq_step_out *out, void *stream) {
+    if (!out || !out->world_action || !d_compact_actions) return fail(JQ_ERR_ARG, "world_action output required");
+    int rc = check_batch(b);
+    if (rc) return rc;
+    rotate_actions_kernel<<<(b->n + 255) / 256, 256, 0, (cudaStream_t)stream>>>(b->n, d_compact_actions, d_seats,
+                                                                             b->turn, out->world_action);
+    CU(cudaGetLastError());
+    return jq_step(b, out->world_action, show_mode, out, stream);
+}
+
+int jq_ply(const jq_batch *b, const int32_t *d_world_actions, int32_t show_mode, const jq_step_out *out,
+           int32_t autoreset, uint64_t seed, uint64_t ply, int32_t *d_counts, int32_t *d_ids, int32_t cap,
+           uint8_t *d_mask, int64_t *d_stats, void *stream) {
+    RuleArgs a;
+    int rc = rules_common(a, b, show_mode, true, stream);
+    if (rc) return rc;
+    if (d_world_actions && (!out || !out->valid)) return fail(JQ_ERR_ARG, "step outputs missing");
+    if (autoreset && !a.pool) return fail(JQ_ERR_NOT_READY, "setup pool not set");
+    if (!d_counts || !d_ids || cap <= 0) return fail(JQ_ERR_ARG, "legal outputs missing");
+    a.acts = d_world_actions;
+    if (out) a.out = *out;
+    a.flags = DO_LEGAL | (d_world_actions ? DO_STEP : 0) | (autoreset ? DO_RESET : 0);
+    a.seed = seed;
+    a.ply = ply;
+    a.counts = d_counts;
+    a.ids = d_ids;
+    a.cap = cap;
+    a.mask = d_mask;
+    a.stats = d_stats;
+    return launch_rules(a, (cudaStream_t)stream);
+}
+
+int jq_legal(const jq_batch *b, const int8_t *d_seats, int32_t *d_counts, int32_t *d_ids, int32_t cap,
+             uint8_t *d_mask, void *stream) {
+    RuleArgs a;
+    int rc = rules_common(a, b, JQ_HALF_DARK, false, stream);
+    if (rc) return rc;
+    if (!d_counts || cap < 0 || (cap > 0 && !d_ids)) return fail(JQ_ERR_ARG, "legal outputs missing");
+    a.flags = DO_LEGAL;
+    a.seats = d_seats;
+    a.counts = d_counts;
+    a.ids = d_ids;
+    a.cap = cap;
+    a.mask = d_mask;
+    return launch_rules(a, (cudaStream_t)stream);
+}
+
+int32_t jq_csr_scratch_ints(int32_t n) { return n <= 0 ? 0 : (n + CSR_BLOCK - 1) / CSR_BLOCK; }
+
+int jq_csr(int32_t n, const int32_t *d_counts, const int32_t *d_ids, int32_t cap, int32_t *d_offsets,
+           int32_t *d_values, int32_t *d_block_scratch, void *stream) {
+    if (n <= 0 || !d_counts || !d_ids || !d_offsets || !d_values || !d_block_scratch || cap <= 0)
+        return fail(JQ_ERR_ARG, "bad CSR arguments");
+    int blocks = jq_csr_scratch_ints(n);
+    cudaStream_t s = (cudaStream_t)stream;
+    csr_partial_kernel<<<blocks, CSR_BLOCK, 0, s>>>(n, d_counts, cap, d_block_scratch);
+    CU(cudaGetLastError());
+    csr_finalize_kernel<<<blocks, CSR_BLOCK, 0, s>>>(n, d_counts, d_ids, cap, d_block_scratch, d_offsets, d_values);
+    CU(cudaGetLastError());
+    return JQ_OK;
+}
+
+int jq_observe(const jq_batch *b, const int8_t *d_observers, int32_t seats_per_env, int32_t show_mode,
+               float *d_spatial, float *d_global, void *stream) {
+    int rc = check_batch(b);
+    if (rc) return rc;
+    if (seats_per_env < 1 || seats_per_env > 4) return fail(JQ_ERR_ARG, "seats_per_env must be 1..4");
+    if (show_mode < 0 || show_mode > 2) return fail(JQ_ERR_ARG, "show_mode must be 0, 1 or 2");
+    if (!d_spatial || !d_global) return fail(JQ_ERR_ARG, "observation outputs missing");
+    if (!d_observers && seats_per_env != 1 && seats_per_env != 4)
+        return fail(JQ_ERR_ARG, "observers required unless seats_per_env is 1 or 4");
+    DeviceState *st;
+    rc = current_dev(st);
+    if (rc) return rc;
+    if (!st->topo || !st->obs) return fail(JQ_ERR_NOT_READY, "jq_init / jq_upload_obs_tables missing");
+    size_t units = (size_t)b->n * seats_per_env;
+    size_t grid = (size_t)st->sms * (st->obs_blocks_per_sm > 0 ? st->obs_blocks_per_sm : 1);
+    if (grid > units) grid = units;
+    obs_kernel<<<(unsigned)grid, OBS_THREADS, obs_smem(), (cudaStream_t)stream>>>(*b, d_observers, seats_per_env,
+                                                                                   show_mode, d_spatial, d_global);
+    CU(cudaGetLastError());
+    return JQ_OK;
+}
+
+int jq_sample_uniform(int32_t n, const int32_t *d_counts, const int32_t *d_ids, int32_t cap, uint64_t seed,
+                      uint64_t ply, int32_t *d_actions, void *stream) {
+    if (n <= 0 || !d_counts || !d_ids || !d_actions || cap <= 0) return fail(JQ_ERR_ARG, "bad sampler arguments");
+    sample_uniform_kernel<<<(n + 255) / 256, 256, 0, (cudaStream_t)stream>>>(n, d_counts, d_ids, cap, seed, ply,
+                                                                            d_actions);
+    CU(cudaGetLastError());
+    return JQ_OK;
+}
+
+int jq_sample_softmax(const jq_batch *b, const int32_t *d_counts, const int32_t *d_ids, int32_t cap, uint64_t seed,
+                      uint64_t ply, int32_t *d_compact_actions, int32_t *d_world_actions, void *stream) {
+    if (!b || b->n <= 0 || !b->turn || !d_counts || !d_ids || cap <= 0) return fail(JQ_ERR_ARG, "bad sampler arguments");
+    sample_softmax_kernel<<<(b->n + 127) / 128, 128, 0, (cudaStream_t)stream>>>(
+        b->n, b->turn, d_counts, d_ids, cap, seed, ply, d_compact_actions, d_world_actions);
+    CU(cudaGetLastError());
+    return JQ_OK;
+}
+
+}  // extern "C"

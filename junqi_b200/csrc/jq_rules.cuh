@@ -1,0 +1,885 @@
+// jq_rules.cuh -- per-env game rules, executed by one warp per env.
+//
+// Semantics are those of junqi_core's BatchedGameState (the state contract):
+//   step_batch / _step_single   batched_state.py:417-613, 739-980
+//   _advance_turn(_vec)         batched_state.py:615-686, 1123-1169
+//   _check_victory(_vec)        batched_state.py:688-733, 1171-1214
+//   legal_action_ids_batch      batched_state.py:370-409 -> move_gen.py:1311-1553
+//   move_requires_gongb         move_gen.py:245-296
+//   apply_combat_event          combat_memory.py:354-562
+//   BeliefTensor.initial/update info_model.py:218-414 (per-piece belief codes)
+//   GameState.new_game          state.py:490-624 (device reset)
+//
+// Layout of the work: lane 0 carries the scalar part of a ply (move or
+// combat, Zobrist, combat memory); the whole warp joins for the collective
+// parts -- the Q12 "has any legal move" checks, seat surrenders, the belief
+// sweep, resets and legal-move generation, where each of lanes 0..29 owns one
+// piece of the acting seat and computes its destination set as a 129-bit
+// mask over the compact board (engineer rail flood-fill as a frontier
+// expansion over per-cell rail-neighbour masks).
+#pragma once
+#include "jq_common.cuh"
+
+namespace jq {
+
+constexpr unsigned FULL = 0xffffffffu;
+
+// ---------------------------------------------------------------------------
+// Device tables (filled by the host API, see jq_api.cu)
+// ---------------------------------------------------------------------------
+__constant__ Topo c_topo;
+__constant__ int64_t c_zturn[4], c_zwin[3], c_zsdead[4], c_zsflag[4], c_zshow[4];
+__constant__ int64_t c_zterm, c_zdraw;
+__device__ int64_t g_zpiece[NP * 14 * NC];
+__device__ int64_t g_zmc[4096];
+__device__ int64_t g_zmslc[512];
+__device__ float g_prior[30 * 12];
+__device__ float g_uniform[12];
+__device__ float g_recency[4 * RECENCY_LEN];
+
+// Zobrist piece term; out-of-range arguments (only reachable from states
+// written by a caller, never by the rules) contribute nothing.
+__device__ __forceinline__ int64_t zpiece(int pid, int t, int f) {
+    if ((unsigned)pid >= (unsigned)NP || (unsigned)t >= 14u || (unsigned)f >= (unsigned)NC) return 0;
+    return g_zpiece[((size_t)pid * 14 + t) * NC + f];
+}
+
+// ---------------------------------------------------------------------------
+// Per-warp shared-memory image of one env
+// ---------------------------------------------------------------------------
+struct StepCtx {
+    int skip, ev, A, D, sf, df, acting, A_type, A_seat, D_type, D_seat;
+    int mc, mslc, new_mc, new_mslc, fcap, fr_src, fr_dst, other_pid, term, win, draw;
+    int new_turn, need_surrender, do_q12, combat;
+    int died_pre[4];
+};
+
+struct __align__(16) WEnv {
+    uint32_t canon[NB][NW];  // canonical-frame destination rows for the mask
+    int32_t scan[32];
+    StepCtx x;
+    int16_t cell[NC + 1];    // flat cell -> pid
+    int16_t posc[NP];        // pid -> compact cell or -1
+    int8_t type[NP];
+    int8_t seat[NP];
+    uint8_t alive[NP];
+    uint8_t sdead[4];
+};
+
+__device__ __forceinline__ size_t PI(int e, int p) { return (size_t)e * NP + p; }
+__device__ __forceinline__ size_t OI(int e, int o, int p) { return ((size_t)e * 4 + o) * NP + p; }
+
+__device__ void warp_load(const jq_batch &b, const Topo &T, WEnv &w, int e, int lane) {
+    for (int f = lane; f < NC; f += 32) {
+        int p = b.cell_pid[(size_t)e * NC + f];
+        w.cell[f] = (int16_t)((p >= 0 && p < NP) ? p : -1);
+    }
+    for (int p = lane; p < NP; p += 32) {
+        size_t q = PI(e, p);
+        w.alive[p] = b.alive[q];
+        w.type[p] = b.piece_type[q];
+        w.seat[p] = b.piece_seat[q];
+        int x = b.pos_x[q], y = b.pos_y[q];
+        w.posc[p] = (int16_t)((x >= 0 && x < 17 && y >= 0 && y < 17) ? T.f2c[y * 17 + x] : -1);
+    }
+    if (lane < 4) w.sdead[lane] = b.seat_dead[(size_t)e * 4 + lane];
+    __syncwarp();
+}
+
+// ---------------------------------------------------------------------------
+// Legal moves
+// ---------------------------------------------------------------------------
+// Destination mask of one piece standing on compact cell c (move_gen.py:
+// 1311-1553 restricted to one candidate piece).
+__device__ void piece_dsts(const Topo &T, int c, int t, const uint32_t *empty, const uint32_t *land,
+                           uint32_t *out) {
+#pragma unroll
+    for (int i = 0; i < NW; ++i) out[i] = 0;
+    if (c < 0 || t == JUNQI || t == DILEI || (T.flags[c] & F_SH)) return;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        int nb = T.adj4[c][k];
+        if (nb != NONE8 && mbit(land, nb)) mset(out, nb);
+        nb = T.diag[c][k];
+        if (nb != NONE8 && mbit(land, nb)) mset(out, nb);
+    }
+    if (!(T.flags[c] & F_RAIL)) return;
+    if (t == GONGB) {
+        // engineer: cells adjacent to the set reached through empty rail cells
+        uint32_t reach[NW], fr[NW], landing[NW];
+#pragma unroll
+        for (int i = 0; i < NW; ++i) reach[i] = fr[i] = landing[i] = 0;
+        mset(reach, c);
+        mset(fr, c);
+        for (int it = 0; it < NB; ++it) {
+            uint32_t nbm[NW] = {0, 0, 0, 0, 0};
+#pragma unroll
+            for (int wd = 0; wd < NW; ++wd) {
+                uint32_t m = fr[wd];
+                while (m) {
+                    int v = wd * 32 + __ffs(m) - 1;
+                    m &= m - 1;
+#pragma unroll
+                    for (int i = 0; i < NW; ++i) nbm[i] |= T.railnb[v][i];
+                }
+            }
+            uint32_t any = 0;
+#pragma unroll
+            for (int i = 0; i < NW; ++i) {
+                landing[i] |= nbm[i] & land[i];
+                uint32_t nw = nbm[i] & empty[i] & ~reach[i];
+                reach[i] |= nw;
+                fr[i] = nw;
+                any |= nw;
+            }
+            if (!any) break;
+        }
+        landing[c >> 5] &= ~(1u << (c & 31));
+#pragma unroll
+        for (int i = 0; i < NW; ++i) out[i] |= landing[i];
+    } else {
+        for (int k = 0; k < 4; ++k)
+            for (int l = 0; l < 12; ++l) {
+                int nb = T.sray[c][k][l];
+                if (nb == NONE8) break;
+                if (mbit(land, nb)) mset(out, nb);
+                if (!mbit(empty, nb)) break;
+            }
+        if (T.flags[c] & F_CURVE_ACTIVE)
+            for (int k = 0; k < 2; ++k)
+                for (int l = 0; l < 11; ++l) {
+                    int nb = T.cray[c][k][l];
+                    if (nb == NONE8) break;
+                    if (mbit(land, nb)) mset(out, nb);
+                    if (!mbit(empty, nb)) break;
+                }
+    }
+}
+
+__device__ __forceinline__ void board_masks(const Topo &T, const WEnv &w, int lane, int team, uint32_t *empty,
+                                            uint32_t *land) {
+#pragma unroll
+    for (int i = 0; i < NW; ++i) {
+        int c = i * 32 + lane;
+        bool em = false, at = false;
+        if (c < NB) {
+            int p = w.cell[T.c2f[c]];
+            em = p < 0;
+            at = p >= 0 && team_of_pid(p) != team && !(T.flags[c] & F_CAMP);
+        }
+        empty[i] = __ballot_sync(FULL, em);
+        land[i] = __ballot_sync(FULL, em || at);
+    }
+}
+
+// Source cell of lane's piece for `seat`, or -1.
+__device__ __forceinline__ int lane_source(const WEnv &w, int lane, int seat) {
+    if (lane >= 30) return -1;
+    int p = seat * 30 + lane;
+    if (!w.alive[p] || w.seat[p] != seat) return -1;
+    return w.posc[p];
+}
+
+// has_legal_moves_soa (move_gen.py:1557-1609): any legal action for `seat`,
+// ignoring terminated / dead flags.
+__device__ bool warp_has_moves(const Topo &T, const WEnv &w, int lane, int seat) {
+    uint32_t empty[NW], land[NW], d[NW];
+    board_masks(T, w, lane, seat & 1, empty, land);
+    int src = lane_source(w, lane, seat);
+    bool any = false;
+    if (src >= 0) {
+        piece_dsts(T, src, w.type[seat * 30 + lane], empty, land, d);
+        any = (d[0] | d[1] | d[2] | d[3] | d[4]) != 0;
+    }
+    return __any_sync(FULL, any);
+}
+
+__device__ __forceinline__ uint4 mask_chunk(const WEnv &w, int j0) {
+    int row = j0 / NB, col = j0 - row * NB;
+    uint32_t v[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        uint32_t bit = row < NB ? (w.canon[row][col >> 5] >> (col & 31)) & 1u : 0u;
+        v[i >> 2] |= bit << ((i & 3) * 8);
+        if (++col == NB) { col = 0; ++row; }
+    }
+    return make_uint4(v[0], v[1], v[2], v[3]);
+}
+
+// Legal actions of `seat` (empty when `skip`), ascending, written to ids
+// (up to cap); optional canonical (16641) byte mask.  Returns the count on
+// every lane.
+__device__ int warp_legal(const Topo &T, WEnv &w, int lane, int seat, bool skip, int32_t *ids, int cap,
+                          uint8_t *mask_env) {
+    uint32_t empty[NW], land[NW], d[NW] = {0, 0, 0, 0, 0};
+    board_masks(T, w, lane, seat & 1, empty, land);
+    int src = skip ? -1 : lane_source(w, lane, seat);
+    if (src >= 0) piece_dsts(T, src, w.type[seat * 30 + lane], empty, land, d);
+    int cnt = __popc(d[0]) + __popc(d[1]) + __popc(d[2]) + __popc(d[3]) + __popc(d[4]);
+    // rank of the source among all sources (compact order == flat order)
+    int rank = 0;
+#pragma unroll
+    for (int i = 0; i < NW; ++i) {
+        uint32_t word = __reduce_or_sync(FULL, (src >= 0 && (src >> 5) == i) ? (1u << (src & 31)) : 0u);
+        if (src >= 0) {
+            if (i < (src >> 5)) rank += __popc(word);
+            else if (i == (src >> 5)) rank += __popc(word & ((1u << (src & 31)) - 1u));
+        }
+    }
+    w.scan[lane] = 0;
+    __syncwarp();
+    if (src >= 0) w.scan[rank] = cnt;
+    __syncwarp();
+    int v = w.scan[lane], inc = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        int t = __shfl_up_sync(FULL, inc, o);
+        if (lane >= o) inc += t;
+    }
+    int total = __shfl_sync(FULL, inc, 31);
+    __syncwarp();
+    w.scan[lane] = inc - v;
+    __syncwarp();
+    if (src >= 0 && ids) {
+        int off = w.scan[rank];
+        int base = T.c2f[src] * NC;
+#pragma unroll
+        for (int i = 0; i < NW; ++i) {
+            uint32_t m = d[i];
+            while (m) {
+                int dc = i * 32 + __ffs(m) - 1;
+                m &= m - 1;
+                if (off < cap) ids[off] = base + T.c2f[dc];
+                ++off;
+            }
+        }
+    }
+    if (mask_env) {
+        for (int k = lane; k < NB * NW; k += 32) (&w.canon[0][0])[k] = 0u;
+        __syncwarp();
+        if (src >= 0) {
+            uint32_t *row = w.canon[T.rot[seat][src]];
+#pragma unroll
+            for (int i = 0; i < NW; ++i) {
+                uint32_t m = d[i];
+                while (m) {
+                    int dc = i * 32 + __ffs(m) - 1;
+                    m &= m - 1;
+                    mset(row, T.rot[seat][dc]);
+                }
+            }
+        }
+        __syncwarp();
+        int head = (int)((16 - ((uintptr_t)mask_env & 15)) & 15);
+        for (int j = lane; j < head; j += 32) {
+            int row = j / NB, col = j - row * NB;
+            mask_env[j] = (uint8_t)((w.canon[row][col >> 5] >> (col & 31)) & 1u);
+        }
+        int body = (MASK_BYTES - head) >> 4;
+        for (int k = lane; k < body; k += 32) {
+            int j0 = head + k * 16;
+            *reinterpret_cast<uint4 *>(mask_env + j0) = mask_chunk(w, j0);
+        }
+        for (int j = head + body * 16 + lane; j < MASK_BYTES; j += 32) {
+            int row = j / NB, col = j - row * NB;
+            mask_env[j] = (uint8_t)((w.canon[row][col >> 5] >> (col & 31)) & 1u);
+        }
+        __syncwarp();
+    }
+    return total;
+}
+
+// ---------------------------------------------------------------------------
+// Path-revealed engineer (move_gen.py:245-296) on the pre-move board, scalar
+// ---------------------------------------------------------------------------
+__device__ bool ray_clear_to(const Topo &T, const WEnv &w, const uint8_t *ray, int n, int dst) {
+    for (int l = 0; l < n; ++l) {
+        int nb = ray[l];
+        if (nb == NONE8) return false;
+        if (nb == dst) return true;
+        if (w.cell[T.c2f[nb]] >= 0) return false;
+    }
+    return false;
+}
+
+__device__ bool engineer_reach(const Topo &T, const WEnv &w, int s, int d) {
+    if (!(T.flags[s] & F_RAIL) || !(T.flags[d] & F_RAIL) || s == d) return false;
+    uint32_t reach[NW] = {0, 0, 0, 0, 0}, fr[NW] = {0, 0, 0, 0, 0};
+    mset(reach, s);
+    mset(fr, s);
+    for (int it = 0; it < NB; ++it) {
+        uint32_t nbm[NW] = {0, 0, 0, 0, 0};
+        for (int wd = 0; wd < NW; ++wd) {
+            uint32_t m = fr[wd];
+            while (m) {
+                int v = wd * 32 + __ffs(m) - 1;
+                m &= m - 1;
+                for (int i = 0; i < NW; ++i) nbm[i] |= T.railnb[v][i];
+            }
+        }
+        if (mbit(nbm, d)) return true;
+        uint32_t any = 0;
+        for (int i = 0; i < NW; ++i) {
+            uint32_t nw = nbm[i] & ~reach[i];
+            uint32_t keep = 0, mm = nw;
+            while (mm) {
+                int v = i * 32 + __ffs(mm) - 1;
+                mm &= mm - 1;
+                if (w.cell[T.c2f[v]] < 0) keep |= 1u << (v & 31);
+            }
+            reach[i] |= keep;
+            fr[i] = keep;
+            any |= keep;
+        }
+        if (!any) break;
+    }
+    return false;
+}
+
+__device__ bool move_requires_gongb(const Topo &T, const WEnv &w, int sf, int df) {
+    if (sf == df) return false;
+    int sx = sf % 17, sy = sf / 17, dx = df % 17, dy = df / 17;
+    int adx = abs(sx - dx), ady = abs(sy - dy);
+    int s = T.f2c[sf], d = T.f2c[df];
+    if (s < 0 || d < 0) return false;
+    if (adx + ady == 1) return false;
+    if (adx == 1 && ady == 1 && ((T.flags[s] & F_CAMP) || (T.flags[d] & F_CAMP))) return false;
+    if (!(T.flags[s] & F_RAIL) || !(T.flags[d] & F_RAIL)) return false;
+    if (sx == dx || sy == dy) {
+        for (int k = 0; k < 4; ++k)
+            if (ray_clear_to(T, w, T.sray[s][k], 12, d)) return false;
+        return engineer_reach(T, w, s, d);
+    }
+    if (T.curve[s] > 0 && T.curve[s] == T.curve[d] && (T.flags[s] & F_CURVE_ACTIVE)) {
+        for (int k = 0; k < 2; ++k)
+            if (ray_clear_to(T, w, T.cray[s][k], 11, d)) return false;
+    }
+    return engineer_reach(T, w, s, d);
+}
+
+// ---------------------------------------------------------------------------
+// Combat memory (combat_memory.py:354-562), scalar on global memory
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void set_pid_bit(uint64_t &lo, uint64_t &hi, int pid) {
+    if (pid < 64) lo |= 1ull << pid;
+    else hi |= 1ull << (pid - 64);
+}
+__device__ __forceinline__ int next_floor(int t) {
+    if (!is_ranked(t)) return 0;
+    int r = 15 - t;
+    return r > 9 ? 9 : r;
+}
+
+__device__ void cm_apply(const jq_batch &b, int e, bool eat, int A, int D, int A_seat, int D_seat, int A_type,
+                         int D_type, int step) {
+    int K = eat ? A : D, V = eat ? D : A, V_seat = eat ? D_seat : A_seat, V_type = eat ? D_type : A_type;
+    int v_idx = tracked_idx(V_type);
+    if (!eat)
+        for (int o = 0; o < 4; ++o)
+            if (b.cm_is_gongb[OI(e, o, V)] || (A_type == GONGB && o == V_seat)) b.cm_atk_gongb[OI(e, o, K)] = 1;
+    for (int o = 0; o < 4; ++o) {
+        size_t k = OI(e, o, K), v = OI(e, o, V);
+        uint64_t lo = b.cm_chain_lo[k] | b.cm_direct_lo[v] | b.cm_chain_lo[v];
+        uint64_t hi = b.cm_chain_hi[k] | b.cm_direct_hi[v] | b.cm_chain_hi[v];
+        set_pid_bit(lo, hi, V);
+        b.cm_chain_lo[k] = lo;
+        b.cm_chain_hi[k] = hi;
+        b.cm_chain_type[k] = (uint16_t)(b.cm_chain_type[k] | b.cm_direct_type[v] | b.cm_chain_type[v]);
+        b.cm_last_chain_step[k] = (int16_t)step;
+        int vf = b.cm_rank_floor[v], prop = vf + 1 < 9 ? vf + 1 : 9;
+        if (vf > 0) {
+            if (prop > b.cm_rank_floor[k]) {
+                b.cm_rank_floor[k] = (int8_t)prop;
+                b.cm_rank_floor_step[k] = (int16_t)step;
+            }
+            b.cm_not_gongb[k] = 1;
+        }
+    }
+    // reverse projection onto observer-own pids (reads V's rows, untouched above)
+    for (int o = 0; o < 4; ++o) {
+        size_t v = OI(e, o, V);
+        uint64_t mlo = 0, mhi = 0;
+        for (int s = 0; s < 30; ++s) set_pid_bit(mlo, mhi, o * 30 + s);
+        uint64_t lo = (b.cm_direct_lo[v] | b.cm_chain_lo[v]) & mlo;
+        uint64_t hi = (b.cm_direct_hi[v] | b.cm_chain_hi[v]) & mhi;
+        if (V_seat == o) set_pid_bit(lo, hi, V);
+        while (lo) {
+            int t = __ffsll((long long)lo) - 1;
+            lo &= lo - 1;
+            size_t tt = OI(e, o, t);
+            uint64_t a = b.cm_eaten_lo[tt], c = b.cm_eaten_hi[tt];
+            set_pid_bit(a, c, K);
+            b.cm_eaten_lo[tt] = a;
+            b.cm_eaten_hi[tt] = c;
+        }
+        while (hi) {
+            int t = 64 + __ffsll((long long)hi) - 1;
+            hi &= hi - 1;
+            if (t >= NP) continue;
+            size_t tt = OI(e, o, t);
+            uint64_t a = b.cm_eaten_lo[tt], c = b.cm_eaten_hi[tt];
+            set_pid_bit(a, c, K);
+            b.cm_eaten_lo[tt] = a;
+            b.cm_eaten_hi[tt] = c;
+        }
+    }
+    for (int o = 0; o < 4; ++o) {
+        size_t k = OI(e, o, K);
+        if (V_seat != o) {
+            int c = b.cm_direct_other[k] + 1;
+            b.cm_direct_other[k] = (int16_t)(c < 32767 ? c : 32767);
+            b.cm_last_direct_step[k] = (int16_t)step;
+            continue;
+        }
+        uint64_t lo = b.cm_direct_lo[k], hi = b.cm_direct_hi[k];
+        set_pid_bit(lo, hi, V);
+        b.cm_direct_lo[k] = lo;
+        b.cm_direct_hi[k] = hi;
+        if (v_idx >= 0) {
+            b.cm_direct_type[k] = (uint16_t)(b.cm_direct_type[k] | (1u << v_idx));
+            b.cm_chain_type[k] = (uint16_t)(b.cm_chain_type[k] | (1u << v_idx));
+        }
+        b.cm_last_direct_step[k] = (int16_t)step;
+        if (eat) {
+            if (V_type == DILEI) b.cm_is_gongb[k] = 1;
+            else b.cm_not_gongb[k] = 1;
+        }
+        if (is_ranked(V_type)) {  // KILLED defender lift and EAT-direct lift use the same rule
+            int pr = next_floor(V_type);
+            if (pr > b.cm_rank_floor[k]) {
+                b.cm_rank_floor[k] = (int8_t)pr;
+                b.cm_rank_floor_step[k] = (int16_t)step;
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Beliefs (info_model.py:218-414)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ bool sees_truth(int obs, int owner, int mode) {
+    if (mode == SM_BRIGHT || obs == owner) return true;
+    return mode == SM_HALF_DARK && ((obs & 1) == (owner & 1));
+}
+__device__ __forceinline__ bool bc_onehot(int c) { return c >= 1 && c <= 12; }
+
+__device__ __forceinline__ uint8_t initial_code(const Topo &T, const WEnv &w, int o, int p, int mode) {
+    if (!w.alive[p]) return BC_NONE;
+    int s = w.seat[p];
+    if (sees_truth(o, s, mode)) return (uint8_t)(tracked_idx(w.type[p]) + 1);
+    if (s >= 0 && s < 4)
+        for (int i = 0; i < 30; ++i)
+            if (T.slot_cell[s][i] == w.posc[p]) return (uint8_t)(BC_PRIOR0 + i);
+    return BC_UNIFORM;
+}
+
+__device__ void warp_belief_init(const jq_batch &b, const Topo &T, const WEnv &w, int e, int lane, int mode) {
+    for (int k = lane; k < 4 * NP; k += 32) {
+        int o = k / NP, p = k - o * NP;
+        b.bel_code[OI(e, o, p)] = initial_code(T, w, o, p, mode);
+    }
+    const int16_t counts[12] = {1, 3, 2, 1, 1, 2, 2, 2, 2, 3, 3, 3};
+    for (int k = lane; k < 16 * 12; k += 32) {
+        int os = k / 12, t = k - os * 12, o = os >> 2, s = os & 3;
+        bool enemy = (s & 1) != (o & 1);
+        b.remaining[(size_t)e * 192 + k] = enemy ? counts[t] : (int16_t)0;
+        if (t == 0) b.rem_tracked[(size_t)e * 16 + os] = enemy;
+    }
+}
+
+__device__ __forceinline__ void rem_dec(const jq_batch &b, int e, int o, int seat, int ti) {
+    if (seat < 0 || seat > 3 || ti < 0) return;
+    size_t tr = (size_t)e * 16 + o * 4 + seat;
+    if (!b.rem_tracked[tr]) return;
+    int16_t *r = &b.remaining[tr * 12 + ti];
+    if (*r > 0) *r = (int16_t)(*r - 1);
+}
+__device__ __forceinline__ void rem_untrack(const jq_batch &b, int e, int o, int seat) {
+    size_t tr = (size_t)e * 16 + o * 4 + seat;
+    b.rem_tracked[tr] = 0;
+    for (int t = 0; t < 12; ++t) b.remaining[tr * 12 + t] = 0;
+}
+
+// Lane o (0..3) applies R3, R5/R7, R4/R6, R1 and R9 for observer o; then the
+// whole warp runs the I5 sweep.
+__device__ void warp_belief_update(const jq_batch &b, const Topo &T, const WEnv &w, int e, int lane,
+                                   const StepCtx &x, int mode, const int *died) {
+    if (lane < 4) {
+        int o = lane;
+        uint8_t *code = b.bel_code + OI(e, o, 0);
+        int a_bel = code[x.A];
+        int d_bel = x.D >= 0 ? code[x.D] : BC_NONE;
+        if (x.fr_src) rem_dec(b, e, o, x.acting, SILING - 2);
+        if (x.fr_dst) rem_dec(b, e, o, x.D_seat, SILING - 2);
+        if (x.ev == EV_EAT && x.D >= 0 && x.D_type == DILEI && a_bel != BC_NONE && !bc_onehot(a_bel)) {
+            code[x.A] = (uint8_t)(GONGB - 1);
+            a_bel = code[x.A];
+            rem_dec(b, e, o, x.acting, GONGB - 2);
+        }
+        if (x.fcap) {
+            if (x.D_seat >= 0 && x.D_seat < 4) rem_untrack(b, e, o, x.D_seat);
+        } else if (x.ev == EV_EAT && x.other_pid >= 0) {
+            int op = x.other_pid;
+            if (code[op] != BC_NONE && !bc_onehot(code[op])) code[op] = (uint8_t)(JUNQI - 1);
+        }
+        a_bel = code[x.A];
+        if (x.ev == EV_EAT) {
+            if (bc_onehot(d_bel)) rem_dec(b, e, o, x.D_seat, d_bel - 1);
+        } else if (x.ev == EV_KILLED) {
+            if (bc_onehot(a_bel)) rem_dec(b, e, o, x.acting, a_bel - 1);
+        } else if (x.ev == EV_BOMB) {
+            if (bc_onehot(a_bel)) rem_dec(b, e, o, x.acting, a_bel - 1);
+            if (bc_onehot(d_bel)) rem_dec(b, e, o, x.D_seat, d_bel - 1);
+        }
+        for (int s = 0; s < 4; ++s)
+            if (died[s]) rem_untrack(b, e, o, s);
+    }
+    __syncwarp();
+    for (int k = lane; k < 4 * NP; k += 32) {
+        int o = k / NP, p = k - o * NP;
+        uint8_t *c = &b.bel_code[OI(e, o, p)];
+        if (!w.alive[p]) { *c = BC_NONE; continue; }
+        if (*c == BC_NONE)
+            *c = sees_truth(o, w.seat[p], mode) ? (uint8_t)(tracked_idx(w.type[p]) + 1) : (uint8_t)BC_UNIFORM;
+    }
+    __syncwarp();
+}
+
+// ---------------------------------------------------------------------------
+// Seat surrender (batched_state.py:1078-1121), warp-parallel; returns the
+// Zobrist delta on every lane.
+// ---------------------------------------------------------------------------
+__device__ int64_t warp_surrender(const jq_batch &b, const Topo &T, WEnv &w, int e, int lane, int seat, int step) {
+    int64_t d = 0;
+    for (int p = lane; p < NP; p += 32) {
+        if (w.seat[p] != seat || !w.alive[p]) continue;
+        size_t q = PI(e, p);
+        int c = w.posc[p];
+        if (c >= 0) {
+            int f = T.c2f[c];
+            d ^= zpiece(p, w.type[p], f);
+            w.cell[f] = -1;
+            b.cell_pid[(size_t)e * NC + f] = -1;
+        }
+        w.alive[p] = 0;
+        w.posc[p] = -1;
+        b.alive[q] = 0;
+        b.pos_x[q] = -1;
+        b.pos_y[q] = -1;
+        b.death_reason[q] = DR_KBE;
+        b.death_step[q] = (int16_t)step;
+        b.death_loc[q] = -1;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) d ^= __shfl_xor_sync(FULL, d, o);
+    if (lane == 0) {
+        w.sdead[seat] = 1;
+        b.seat_dead[(size_t)e * 4 + seat] = 1;
+    }
+    __syncwarp();
+    return d ^ c_zsdead[seat];
+}
+
+// ---------------------------------------------------------------------------
+// Reset to GameState.new_game(lineup) (state.py:490-624), warp-parallel
+// ---------------------------------------------------------------------------
+__device__ void warp_reset(const jq_batch &b, const Topo &T, WEnv &w, int e, int lane, const int8_t *lineup, int mode) {
+    for (int f = lane; f < NC; f += 32) {
+        w.cell[f] = -1;
+        b.cell_pid[(size_t)e * NC + f] = -1;
+    }
+    __syncwarp();
+    int64_t z = 0;
+    for (int p = lane; p < NP; p += 32) {
+        size_t q = PI(e, p);
+        int t = lineup ? lineup[p] : 0;
+        bool real = t != NONE;
+        int s = p / 30, c = T.slot_cell[s][p % 30], f = T.c2f[c];
+        int x = f % 17, y = f / 17;
+        b.alive[q] = real;
+        b.piece_type[q] = real ? (int8_t)t : (int8_t)-1;
+        b.piece_seat[q] = real ? (int8_t)s : (int8_t)-1;
+        b.pos_x[q] = b.zero_x[q] = real ? (int8_t)x : (int8_t)-1;
+        b.pos_y[q] = b.zero_y[q] = real ? (int8_t)y : (int8_t)-1;
+        b.move_count[q] = 0;
+        b.active_eat[q] = 0;
+        b.passive_surv[q] = 0;
+        b.death_reason[q] = -1;
+        b.death_step[q] = -1;
+        b.death_loc[q] = -1;
+        w.alive[p] = real;
+        w.type[p] = real ? (int8_t)t : (int8_t)-1;
+        w.seat[p] = real ? (int8_t)s : (int8_t)-1;
+        w.posc[p] = (int16_t)(real ? c : -1);
+        if (real) {
+            w.cell[f] = (int16_t)p;
+            b.cell_pid[(size_t)e * NC + f] = (int16_t)p;
+            z ^= zpiece(p, t, f);
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) z ^= __shfl_xor_sync(FULL, z, o);
+    if (lane < 4) {
+        w.sdead[lane] = 0;
+        b.seat_dead[(size_t)e * 4 + lane] = 0;
+        b.seat_flag[(size_t)e * 4 + lane] = 0;
+    }
+    if (lane == 0) {
+        b.turn[e] = 0;
+        b.zobrist[e] = z ^ c_zturn[0] ^ g_zmc[0] ^ g_zmslc[0] ^ c_zwin[0] ^ c_zshow[mode & 3];
+        b.move_counter[e] = 0;
+        b.mslc[e] = 0;
+        b.terminated[e] = 0;
+        b.winner[e] = -1;
+        b.draw[e] = 0;
+        b.hist_count[e] = 0;
+    }
+    for (int k = lane; k < 4 * NP; k += 32) {
+        size_t q = (size_t)e * 4 * NP + k;
+        b.cm_direct_lo[q] = 0; b.cm_direct_hi[q] = 0; b.cm_direct_type[q] = 0;
+        b.cm_last_direct_step[q] = -1; b.cm_direct_other[q] = 0;
+        b.cm_chain_lo[q] = 0; b.cm_chain_hi[q] = 0; b.cm_chain_type[q] = 0;
+        b.cm_last_chain_step[q] = -1; b.cm_eaten_lo[q] = 0; b.cm_eaten_hi[q] = 0;
+        b.cm_rank_floor[q] = 0; b.cm_rank_floor_step[q] = -1;
+        b.cm_is_gongb[q] = 0; b.cm_not_gongb[q] = 0; b.cm_atk_gongb[q] = 0;
+    }
+    b.hist_src[(size_t)e * HIST + lane] = -1;
+    b.hist_dst[(size_t)e * HIST + lane] = -1;
+    __syncwarp();
+    warp_belief_init(b, T, w, e, lane, mode);
+    __syncwarp();
+}
+
+// ---------------------------------------------------------------------------
+// One ply (BatchedGameState.step_batch for one env)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int resolve_combat(int a, int d) {
+    if (a <= DARK || d <= DARK || a > GONGB || d > GONGB) return 0;
+    if (a == JUNQI || a == DILEI) return 0;  // the reference raises here
+    if (a == ZHADAN || d == ZHADAN) return EV_BOMB;
+    if (d == JUNQI) return EV_EAT;
+    if (d == DILEI) return a == GONGB ? EV_EAT : EV_KILLED;
+    if (a == d) return EV_BOMB;
+    return a < d ? EV_EAT : EV_KILLED;
+}
+
+__device__ __forceinline__ void check_victory(const WEnv &w, int acting, int mc, int mslc, int &term, int &win,
+                                              int &draw) {
+    bool red = !w.sdead[0] || !w.sdead[2], blue = !w.sdead[1] || !w.sdead[3];
+    term = 0; win = -1; draw = 0;
+    if (!red && !blue) { term = 1; win = acting % 2; return; }
+    if (!red) { term = 1; win = 1; return; }
+    if (!blue) { term = 1; win = 0; return; }
+    if (mc >= 4000 || mslc >= 200) { term = 1; draw = 1; }
+}
+
+__device__ __forceinline__ void kill_piece(const jq_batch &b, const Topo &T, WEnv &w, int e, int pid, int cell_f,
+                                           int reason, int step, int loc) {
+    if (!w.alive[pid]) return;
+    size_t q = PI(e, pid);
+    w.alive[pid] = 0;
+    w.posc[pid] = -1;
+    w.cell[cell_f] = -1;
+    b.alive[q] = 0;
+    b.cell_pid[(size_t)e * NC + cell_f] = -1;
+    b.pos_x[q] = -1;
+    b.pos_y[q] = -1;
+    b.death_reason[q] = (int8_t)reason;
+    b.death_step[q] = (int16_t)step;
+    b.death_loc[q] = (int16_t)loc;
+}
+
+__device__ __forceinline__ void move_piece(const jq_batch &b, const Topo &T, WEnv &w, int e, int pid, int sf, int df) {
+    size_t q = PI(e, pid);
+    w.cell[sf] = -1;
+    w.cell[df] = (int16_t)pid;
+    w.posc[pid] = T.f2c[df];
+    b.cell_pid[(size_t)e * NC + sf] = -1;
+    b.cell_pid[(size_t)e * NC + df] = (int16_t)pid;
+    b.pos_x[q] = (int8_t)(df % 17);
+    b.pos_y[q] = (int8_t)(df / 17);
+}
+
+// Returns true on every lane when the ply was applied.
+__device__ bool warp_step(const jq_batch &b, const Topo &T, WEnv &w, int e, int lane, int32_t act, int mode,
+                          const jq_step_out &out, int64_t *stats) {
+    StepCtx &x = w.x;
+    int64_t zob = 0;
+    if (lane == 0) {
+        x.skip = 1;
+        int term0 = b.terminated[e];
+        out.valid[e] = 0;
+        if (out.event) out.event[e] = 0;
+        if (out.terminated) out.terminated[e] = (uint8_t)term0;
+        if (out.winner) out.winner[e] = b.winner[e];
+        if (out.draw) out.draw[e] = b.draw[e];
+        if (out.flag_captured) out.flag_captured[e] = 0;
+        if (out.reward) out.reward[e] = 0.f;
+        if (!term0 && act >= 0 && act < NC * NC) {
+            int sf = act / NC, df = act % NC, A = w.cell[sf], D = w.cell[df];
+            if (A >= 0 && sf != df) {
+                x.sf = sf; x.df = df; x.A = A; x.D = D;
+                x.A_type = w.type[A]; x.A_seat = w.seat[A];
+                x.D_type = D >= 0 ? w.type[D] : 0;
+                x.D_seat = D >= 0 ? w.seat[D] : -1;
+                x.ev = D < 0 ? EV_MOVE : resolve_combat(x.A_type, x.D_type);
+                if (x.ev) x.skip = 0;
+            }
+        }
+    }
+    __syncwarp();
+    if (x.skip) return false;
+    if (lane == 0) {
+        const int sf = x.sf, df = x.df, A = x.A, D = x.D;
+        x.acting = b.turn[e];
+        x.mc = b.move_counter[e];
+        x.mslc = b.mslc[e];
+        x.new_mc = x.mc + 1;
+        x.combat = D >= 0;
+        for (int s = 0; s < 4; ++s) x.died_pre[s] = w.sdead[s];
+        x.other_pid = -1;
+        x.fcap = x.fr_src = x.fr_dst = 0;
+        x.need_surrender = 0;
+        if (D >= 0 && x.D_seat >= 0 && x.D_seat < 4) {
+            int s0 = T.c2f[T.slot_cell[x.D_seat][26]], s1 = T.c2f[T.slot_cell[x.D_seat][28]];
+            if (df == s0) x.other_pid = w.cell[s1];
+            else if (df == s1) x.other_pid = w.cell[s0];
+        }
+        if (x.A_type == GONGB) {
+            int adx = abs(sf % 17 - df % 17), ady = abs(sf / 17 - df / 17);
+            if ((D >= 0 || adx + ady > 1) && move_requires_gongb(T, w, sf, df))
+                for (int o = 0; o < 4; ++o) b.cm_is_gongb[OI(e, o, A)] = 1;
+        }
+        zob = b.zobrist[e] ^ c_zturn[x.acting & 3] ^ g_zmc[x.mc & 0xFFF] ^ g_zmslc[x.mslc & 0x1FF];
+        if (D < 0) {
+            zob ^= zpiece(A, x.A_type, sf) ^ zpiece(A, x.A_type, df);
+            move_piece(b, T, w, e, A, sf, df);
+            b.move_count[PI(e, A)]++;
+            x.new_mslc = x.mslc + 1;
+        } else {
+            int ds = x.new_mc;
+            x.fr_src = x.A_type == SILING && (x.ev == EV_KILLED || x.ev == EV_BOMB);
+            x.fr_dst = x.D_type == SILING && (x.ev == EV_EAT || x.ev == EV_BOMB);
+            if (x.fr_src && x.A_seat >= 0 && x.A_seat < 4 && !b.seat_flag[(size_t)e * 4 + x.A_seat]) {
+                b.seat_flag[(size_t)e * 4 + x.A_seat] = 1;
+                zob ^= c_zsflag[x.A_seat];
+            }
+            if (x.fr_dst && x.D_seat >= 0 && x.D_seat < 4 && !b.seat_flag[(size_t)e * 4 + x.D_seat]) {
+                b.seat_flag[(size_t)e * 4 + x.D_seat] = 1;
+                zob ^= c_zsflag[x.D_seat];
+            }
+            x.fcap = x.D_type == JUNQI;
+            if (x.ev == EV_EAT) {
+                zob ^= zpiece(D, x.D_type, df);
+                kill_piece(b, T, w, e, D, df, DR_KBE, ds, df);
+                zob ^= zpiece(A, x.A_type, sf) ^ zpiece(A, x.A_type, df);
+                move_piece(b, T, w, e, A, sf, df);
+                b.active_eat[PI(e, A)]++;
+                cm_apply(b, e, true, A, D, x.A_seat, x.D_seat, x.A_type, x.D_type, ds);
+            } else if (x.ev == EV_KILLED) {
+                int dr = (x.D_type == DILEI || x.D_type == ZHADAN) ? DR_MINE : DR_KBE;
+                zob ^= zpiece(A, x.A_type, sf);
+                kill_piece(b, T, w, e, A, sf, dr, ds, df);
+                b.passive_surv[PI(e, D)]++;
+                cm_apply(b, e, false, A, D, x.A_seat, x.D_seat, x.A_type, x.D_type, ds);
+            } else {
+                zob ^= zpiece(A, x.A_type, sf) ^ zpiece(D, x.D_type, df);
+                kill_piece(b, T, w, e, A, sf, DR_MUTUAL, ds, df);
+                kill_piece(b, T, w, e, D, df, DR_MUTUAL, ds, df);
+            }
+            x.new_mslc = 0;
+            if (x.fcap && x.D_seat >= 0 && x.D_seat < 4 && !w.sdead[x.D_seat]) {
+                if (!b.seat_flag[(size_t)e * 4 + x.D_seat]) {
+                    b.seat_flag[(size_t)e * 4 + x.D_seat] = 1;
+                    zob ^= c_zsflag[x.D_seat];
+                }
+                x.need_surrender = 1;
+            }
+        }
+    }
+    __syncwarp();
+    if (x.need_surrender) {
+        int64_t d = warp_surrender(b, T, w, e, lane, x.D_seat, x.new_mc);
+        if (lane == 0) zob ^= d;
+    }
+    if (x.combat) {
+        // post-combat dead sweep (batched_state.py:893-902)
+        for (int s = 0; s < 4; ++s) {
+            if (w.sdead[s]) continue;
+            bool any = false;
+            for (int p = lane; p < NP; p += 32) any |= (w.seat[p] == s && w.alive[p]);
+            if (!__any_sync(FULL, any)) {
+                if (lane == 0) {
+                    w.sdead[s] = 1;
+                    b.seat_dead[(size_t)e * 4 + s] = 1;
+                    zob ^= c_zsdead[s];
+                }
+                __syncwarp();
+            }
+        }
+    }
+    if (lane == 0) {
+        check_victory(w, x.acting, x.new_mc, x.new_mslc, x.term, x.win, x.draw);
+        int cand = (x.acting + 1) & 3;
+        // plain moves test Q12 only past a dead next seat (batched_state.py:636-684)
+        x.do_q12 = x.combat ? !x.term : (int)w.sdead[cand];
+        x.new_turn = x.combat ? (x.term ? x.acting : (x.acting + 1) & 3) : cand;
+    }
+    __syncwarp();
+    if (x.do_q12) {
+        int cand = (x.acting + 1) & 3, chain = 0;
+        bool found = false;
+        while (chain < 4) {
+            if (w.sdead[cand]) { cand = (cand + 1) & 3; ++chain; continue; }
+            if (warp_has_moves(T, w, lane, cand)) { found = true; break; }
+            int64_t d = warp_surrender(b, T, w, e, lane, cand, x.new_mc);
+            if (lane == 0) zob ^= d;
+            cand = (cand + 1) & 3;
+            ++chain;
+        }
+        if (lane == 0) {
+            x.new_turn = x.combat ? (found ? cand : (x.acting + 1) & 3) : cand;
+            check_victory(w, x.acting, x.new_mc, x.new_mslc, x.term, x.win, x.draw);
+        }
+    }
+    __syncwarp();
+    if (lane == 0) {
+        zob ^= g_zmc[x.new_mc & 0xFFF] ^ g_zmslc[x.new_mslc & 0x1FF] ^ c_zturn[x.new_turn & 3];
+        if (x.term) zob ^= c_zterm;
+        if (x.draw) zob ^= c_zdraw;
+        if (x.win >= 0) zob ^= c_zwin[0] ^ c_zwin[x.win + 1];
+        b.move_counter[e] = x.new_mc;
+        b.mslc[e] = x.new_mslc;
+        b.turn[e] = (int8_t)x.new_turn;
+        b.zobrist[e] = zob;
+        b.terminated[e] = (uint8_t)x.term;
+        b.winner[e] = (int8_t)x.win;
+        b.draw[e] = (uint8_t)x.draw;
+        out.valid[e] = 1;
+        if (out.event) out.event[e] = (int8_t)x.ev;
+        if (out.terminated) out.terminated[e] = (uint8_t)x.term;
+        if (out.winner) out.winner[e] = (int8_t)x.win;
+        if (out.draw) out.draw[e] = (uint8_t)x.draw;
+        if (out.flag_captured) out.flag_captured[e] = (uint8_t)x.fcap;
+        if (out.reward)
+            out.reward[e] = (x.term && !x.draw && x.win >= 0) ? (((x.acting & 1) == x.win) ? 1.f : -1.f) : 0.f;
+        int hc = b.hist_count[e];
+        b.hist_src[(size_t)e * HIST + (hc & (HIST - 1))] = (int16_t)x.sf;
+        b.hist_dst[(size_t)e * HIST + (hc & (HIST - 1))] = (int16_t)x.df;
+        b.hist_count[e] = hc + 1;
+        if (stats && x.term) {
+            if (x.draw) atomicAdd((unsigned long long *)&stats[2], 1ull);
+            else if (x.win >= 0) atomicAdd((unsigned long long *)&stats[x.win], 1ull);
+            atomicAdd((unsigned long long *)&stats[3], 1ull);
+            atomicAdd((unsigned long long *)&stats[4], (unsigned long long)x.new_mc);
+        }
+    }
+    __syncwarp();
+    int died[4];
+#pragma unroll
+    for (int s = 0; s < 4; ++s) died[s] = w.sdead[s] && !x.died_pre[s];
+    warp_belief_update(b, T, w, e, lane, x, mode, died);
+    return true;
+}
+
+}  // namespace jq
