@@ -190,6 +190,20 @@ int32_t jq_csr_scratch_ints(int32_t n);
 int jq_csr(int32_t n, const int32_t *d_counts, const int32_t *d_ids, int32_t cap,
            int32_t *d_offsets, int32_t *d_values, int32_t *d_block_scratch, void *stream);
 
+/* Allocation-free variant of jq_csr for callers that cannot allocate device
+ * memory (a process whose CUDA allocator already owns the HBM budget, or a
+ * thin FFI host holding only the buffers it was given).  No counterpart in
+ * the reference.  The block-sum scratch is a 4 KiB file-scope device array
+ * shared by every call on a GPU, so n is limited to JQ_NOALLOC_MAX_ENVS
+ * (larger n returns JQ_ERR_CAPACITY) and calls that overlap on the GPU
+ * (different streams without ordering) race on it.  The first call on a
+ * device looks up the array's device address (cudaGetSymbolAddress) with
+ * that device current; make that first call before any stream capture.
+ * Calls no cudaMalloc / cudaFree or allocating library routine. */
+#define JQ_NOALLOC_MAX_ENVS (1 << 20)
+int jq_csr_noalloc(int32_t n, const int32_t *d_counts, const int32_t *d_ids, int32_t cap,
+                   int32_t *d_offsets, int32_t *d_values, void *stream);
+
 /* 317-channel observation for `seats_per_env` observers per env:
  * d_observers is (N, seats_per_env) int8 (NULL with seats_per_env==1 means
  * each env's turn; NULL with 4 means seats 0..3).  Writes d_spatial

@@ -493,6 +493,51 @@ int jq_csr(int32_t n, const int32_t *d_counts, const int32_t *d_ids, int32_t cap
     return JQ_OK;
 }
 
+// ---------------------------------------------------------------------------
+// Allocation-free CSR.  Some hosts of this library cannot allocate device
+// memory: a training process whose PyTorch caching allocator has reserved
+// the whole HBM budget, or a thin FFI host (a game server or evaluation
+// harness calling through ctypes / cgo) that owns only the buffers it was
+// handed and has no CUDA allocator of its own.  jq_csr_noalloc keeps its
+// block-sum scratch in the file-scope array below instead of asking the
+// caller for it, and calls no allocating routine.  The array holds one int
+// per 1024 envs, so it covers up to JQ_NOALLOC_MAX_ENVS envs; every GPU that
+// loads libjq.so holds these 4 KiB until the process exits.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) int32_t g_noalloc_scratch[(JQ_NOALLOC_MAX_ENVS + CSR_BLOCK - 1) / CSR_BLOCK];
+static int32_t *g_noalloc_ptr[MAX_DEV];  // device address of g_noalloc_scratch, per device
+
+int jq_csr_noalloc(int32_t n, const int32_t *d_counts, const int32_t *d_ids, int32_t cap, int32_t *d_offsets,
+                   int32_t *d_values, void *stream) {
+    if (n <= 0 || !d_counts || !d_ids || !d_offsets || !d_values || cap <= 0)
+        return fail(JQ_ERR_ARG, "bad CSR arguments");
+    if (n > JQ_NOALLOC_MAX_ENVS) return fail(JQ_ERR_CAPACITY, "jq_csr_noalloc: n exceeds JQ_NOALLOC_MAX_ENVS");
+    int dev = 0;
+    CU(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= MAX_DEV) return fail(JQ_ERR_ARG, "device index out of range");
+    int32_t *scratch;
+    {
+        // First call on a device: look up the array's device address with that
+        // device current.  The host-side symbol itself is only a stand-in.
+        std::lock_guard<std::mutex> lk(g_mu);
+        if (!g_noalloc_ptr[dev]) {
+            void *p = nullptr;
+            CU(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+            g_noalloc_ptr[dev] = static_cast<int32_t *>(p);
+        }
+        scratch = g_noalloc_ptr[dev];
+    }
+    // csr_partial_kernel writes every block sum csr_finalize_kernel reads, so
+    // the contents left by the previous call need no clearing.
+    int blocks = jq_csr_scratch_ints(n);
+    cudaStream_t s = (cudaStream_t)stream;
+    csr_partial_kernel<<<blocks, CSR_BLOCK, 0, s>>>(n, d_counts, cap, scratch);
+    CU(cudaGetLastError());
+    csr_finalize_kernel<<<blocks, CSR_BLOCK, 0, s>>>(n, d_counts, d_ids, cap, scratch, d_offsets, d_values);
+    CU(cudaGetLastError());
+    return JQ_OK;
+}
+
 int jq_observe(const jq_batch *b, const int8_t *d_observers, int32_t seats_per_env, int32_t show_mode,
                float *d_spatial, float *d_global, void *stream) {
     int rc = check_batch(b);
