@@ -45,6 +45,14 @@ CONFIGS = {
 
 OBS_WRITE = 317 * 289 * 4 + 28 * 4  # bytes written per (env, seat) observation
 
+# jq_batch.rules: 1 = GameState.step (state.py; Q12 "no legal move -> seat
+# dies" on every ply, as the single-env JunqiEnv and the reference GPU kernel
+# do), 0 = BatchedGameState.step_batch (batched_state.py; plain moves test Q12
+# only when the next seat is already dead, so a seat left without moves can
+# stall its env for good).  Both are pinned bit-exactly to junqi_core.
+RULES = {"gamestate": 1, "batched": 0}
+RULES_TEXT = {"gamestate": "GameState.step (state.py:638)", "batched": "BatchedGameState.step_batch (batched_state.py:417)"}
+
 
 def obs_read_bytes() -> int:
     """Bytes the observation kernel must read per (env, observer) unit."""
@@ -119,13 +127,13 @@ def profiled_traffic(cfg: str) -> float | None:
 # CPU arms (oracle = CPU restatement of the reference rules)
 # ---------------------------------------------------------------------------
 
-def cpu_rollout(envs: int, plies: int, seats: int, seed: int, threads: int, budget_s: float):
+def cpu_rollout(envs: int, plies: int, seats: int, seed: int, threads: int, budget_s: float, rules: int = 1):
     """Step + legal + observation on the CPU oracle; returns (plies/s, plies, seconds, sample text)."""
     os.environ["JQ_ORACLE_THREADS"] = str(threads)
     from junqi_b200 import tables
     from oracle import oracle as O
     pool = tables.build_setup_pool(256, seed=42)
-    b = O.OracleBatch(envs, 2)
+    b = O.OracleBatch(envs, 2, rules=rules)
     b.threads = threads
     rng = np.random.default_rng(seed)
     for e in range(envs):
@@ -170,13 +178,15 @@ def reference_arm(args, cfg: dict) -> None:
     O.build()
     envs = min(cfg["envs"], 256 * threads)
     for _ in range(args.warmup if args.warmup < 3 else 2):
-        cpu_rollout(min(envs, 64), 1, cfg["seats"], args.seed, threads, 5.0)
-    rate, done, dt, sample = cpu_rollout(envs, args.steps, cfg["seats"], args.seed, threads, 120.0)
+        cpu_rollout(min(envs, 64), 1, cfg["seats"], args.seed, threads, 5.0, RULES[args.rules])
+    rate, done, dt, sample = cpu_rollout(envs, args.steps, cfg["seats"], args.seed, threads, 120.0,
+                                         RULES[args.rules])
     line = {"impl": "reference", "metric": "env plies/s (step + legal mask + 317-ch obs)", "value": rate,
             "unit": "plies/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8/int16/f32",
             "data": "synthetic (seeded setup pool, uniform-random legal policy)",
-            "config": {"workload": cfg["workload"], "envs_sampled": envs, "seats_per_env": cfg["seats"]},
+            "config": {"workload": cfg["workload"], "envs_sampled": envs, "seats_per_env": cfg["seats"],
+                       "rules": RULES_TEXT[args.rules]},
             "cpu_baseline": {"value": rate, "unit": "plies/s", "cores": threads, "kind": "port",
                              "sample": sample + f", {dt:.1f} s"},
             "e2e": {"value": rate, "unit": "plies/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -199,6 +209,8 @@ def main() -> None:
     ap.add_argument("--seed", type=int, default=2026)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--rules", default="gamestate", choices=sorted(RULES),
+                    help="turn-advance rules: GameState.step (default) or BatchedGameState.step_batch")
     args = ap.parse_args()
     cfg = dict(CONFIGS[args.config])
     if args.envs:
@@ -228,7 +240,8 @@ def main() -> None:
     n, seats = cfg["envs"], cfg["seats"]
     seed = args.seed + rank * 10_000
     pool = tables.build_setup_pool(cfg["pool"], seed=42)
-    env = JunqiEnvB200(n, device=local, show_mode=cfg["mode"], pool=pool, obs_seats=seats)
+    env = JunqiEnvB200(n, device=local, show_mode=cfg["mode"], pool=pool, obs_seats=seats,
+                       rules=RULES[args.rules])
     sampler = env.sample_uniform if cfg["policy"] == "uniform" else env.sample_softmax
     env.reset(seed=seed)
     stream = torch.cuda.current_stream()
@@ -247,10 +260,11 @@ def main() -> None:
             ev[3].record(stream)
         return env.out["valid"]
 
-    for t in range(1, args.warmup + 1):
-        one_ply(t)
+    applied = torch.zeros(n, dtype=torch.int32, device=env.device)
+    for t in range(1, args.warmup + 1):  # same ops as the timed loop, so every kernel is loaded
+        applied += one_ply(t)
     env.stats.zero_()
-    applied = torch.zeros((), dtype=torch.int64, device=env.device)
+    applied.zero_()
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     clock_rows, stop = [], threading.Event()
@@ -264,7 +278,7 @@ def main() -> None:
     start.record(stream)
     for k in range(args.steps):
         t = args.warmup + 1 + k
-        applied += one_ply(t, evs[k]).sum(dtype=torch.int64)
+        applied += one_ply(t, evs[k])
     if world > 1:
         dist.all_reduce(env.stats)  # one collective per rollout: episode statistics
     end.record(stream)
@@ -277,7 +291,7 @@ def main() -> None:
     ms_total = start.elapsed_time(end)
     obs_ms = [e[0].elapsed_time(e[1]) for e in evs]
     ply_ms = [e[2].elapsed_time(e[3]) for e in evs]
-    plies_local = int(applied.item())
+    plies_local = int(applied.sum(dtype=torch.int64).item())
     t_max = torch.tensor([ms_total], dtype=torch.float64, device=env.device)
     tot = torch.tensor([plies_local], dtype=torch.int64, device=env.device)
     if world > 1:
@@ -307,6 +321,7 @@ def main() -> None:
             "data": "synthetic (seeded setup pool of random legal lineups, seeded policy)",
             "config": {"workload": cfg["workload"], "envs_per_gpu": n, "seats_per_env": seats,
                        "policy": cfg["policy"], "show_mode": "HALF_DARK", "plies_applied": plies_all,
+                       "plies_offered": n * world * args.steps, "rules": RULES_TEXT[args.rules],
                        "l2": "per-step output (obs) > 1.5 GB >> 126 MB L2; no flush needed",
                        "parallelism": f"env-sharded x{world} (weak)"},
             "roofline": {"bound": "hbm", "kernel": "obs_kernel", "achieved": achieved, "peak": peak,
@@ -315,7 +330,7 @@ def main() -> None:
                          "algorithmic_bytes_per_launch": obs_bytes, "avg_launch_ms": obs_avg,
                          "ply_kernel_avg_ms": statistics.mean(ply_ms)},
             "clocks": summarize_clocks(clock_rows),
-            "gpu_launches": 3 * args.steps,
+            "gpu_launches": 3 * args.steps,  # obs_kernel + sample kernel + rules_kernel per ply
             "episode_stats": {"wins_team0": stats[0], "wins_team1": stats[1], "draws": stats[2],
                               "episodes": stats[3], "sum_len": stats[4]},
             "wall_s": t_wall,
@@ -324,7 +339,8 @@ def main() -> None:
             line["e2e"] = e2e
         if not args.no_cpu_baseline:
             threads = host_cores()
-            rate, done, dt, sample = cpu_rollout(min(n, 64 * threads), 400, seats, args.seed, threads, 15.0)
+            rate, done, dt, sample = cpu_rollout(min(n, 64 * threads), 400, seats, args.seed, threads, 15.0,
+                                                 RULES[args.rules])
             line["cpu_baseline"] = {"value": rate, "unit": "plies/s", "cores": threads, "kind": "port",
                                     "sample": sample + f", {dt:.1f} s"}
         print(json.dumps(line), flush=True)

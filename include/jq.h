@@ -16,7 +16,7 @@
 #include <stddef.h>
 #include <stdint.h>
 
-#define JQ_ABI_VERSION 1
+#define JQ_ABI_VERSION 2
 
 #define JQ_NUM_PIECES 120
 #define JQ_NUM_CELLS 289
@@ -38,6 +38,15 @@ enum {
     JQ_ERR_NOT_READY = 3, /* jq_init / table uploads missing on this device */
     JQ_ERR_CAPACITY = 4   /* an output buffer is too small */
 };
+
+/* Rule sets (jq_batch.rules).  JQ_RULES_BATCHED follows BatchedGameState
+ * (batched_state.py): after a plain move the Q12 "no legal move -> seat
+ * dies" test only runs past an already-dead next seat, and surrendered
+ * pieces get death_loc -1.  JQ_RULES_GAMESTATE follows GameState.step_inplace
+ * (state.py:309-669), which the single-env JunqiEnv and the reference's GPU
+ * rollout also follow: Q12 after every ply, victory checked before the turn
+ * advances, surrendered pieces keep their current cell as death_loc. */
+enum { JQ_RULES_BATCHED = 0, JQ_RULES_GAMESTATE = 1 };
 
 /* Show modes (junqi_core/rules.py:598-603). */
 enum { JQ_BRIGHT = 0, JQ_DARK = 1, JQ_HALF_DARK = 2 };
@@ -80,6 +89,7 @@ typedef struct jq_batch {
     uint8_t *bel_code;                 /* (4,120) per-observer belief code */
     int16_t *remaining;                /* (4,4,12) per-observer enemy inventory */
     uint8_t *rem_tracked;              /* (4,4)  bool */
+    int32_t rules;                     /* JQ_RULES_BATCHED or JQ_RULES_GAMESTATE */
 } jq_batch;
 
 /* Per-env step outputs (N each); any pointer may be NULL except valid. */

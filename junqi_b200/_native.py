@@ -41,7 +41,11 @@ BATCH_FIELDS = [
 
 
 class JqBatch(ctypes.Structure):
-    _fields_ = [("n", ctypes.c_int32)] + [(n, ctypes.c_void_p) for n, _ in BATCH_FIELDS]
+    _fields_ = [("n", ctypes.c_int32)] + [(n, ctypes.c_void_p) for n, _ in BATCH_FIELDS] + \
+        [("rules", ctypes.c_int32)]
+
+
+RULES_BATCHED, RULES_GAMESTATE = 0, 1
 
 
 class JqStepOut(ctypes.Structure):

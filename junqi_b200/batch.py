@@ -51,7 +51,7 @@ BYTES_PER_ENV = sum(int(np.dtype(dt).itemsize * np.prod(sh, dtype=np.int64)) for
 class DeviceBatch:
     """N envs of device state in the jq_batch layout."""
 
-    def __init__(self, n: int, device: torch.device | str | int = "cuda"):
+    def __init__(self, n: int, device: torch.device | str | int = "cuda", rules: int = N.RULES_BATCHED):
         if n <= 0:
             raise ValueError(f"num_envs must be positive, got {n}")
         self.n = int(n)
@@ -61,8 +61,19 @@ class DeviceBatch:
             self.t[name] = torch.full((self.n,) + shape, fill, dtype=_STORAGE[dt], device=self.device)
         self._struct = N.JqBatch()
         self._struct.n = self.n
+        self._struct.rules = int(rules)
         for name, _, _, _ in FIELDS:
             setattr(self._struct, name, self.t[name].data_ptr())
+
+    @property
+    def rules(self) -> int:
+        return int(self._struct.rules)
+
+    @rules.setter
+    def rules(self, r: int) -> None:
+        if r not in (N.RULES_BATCHED, N.RULES_GAMESTATE):
+            raise ValueError(f"unknown rule set {r}")
+        self._struct.rules = int(r)
 
     @property
     def struct(self) -> N.JqBatch:

@@ -50,7 +50,7 @@ __device__ __forceinline__ int64_t zpiece(int pid, int t, int f) {
 struct StepCtx {
     int skip, ev, A, D, sf, df, acting, A_type, A_seat, D_type, D_seat;
     int mc, mslc, new_mc, new_mslc, fcap, fr_src, fr_dst, other_pid, term, win, draw;
-    int new_turn, need_surrender, do_q12, combat;
+    int new_turn, need_surrender, do_q12, combat, full_advance;
     int died_pre[4];
 };
 
@@ -551,10 +551,12 @@ __device__ void warp_belief_update(const jq_batch &b, const Topo &T, const WEnv 
 // ---------------------------------------------------------------------------
 __device__ int64_t warp_surrender(const jq_batch &b, const Topo &T, WEnv &w, int e, int lane, int seat, int step) {
     int64_t d = 0;
+    const bool keep_loc = b.rules == JQ_RULES_GAMESTATE;  // state.py:640-693 records the current cell
     for (int p = lane; p < NP; p += 32) {
         if (w.seat[p] != seat || !w.alive[p]) continue;
         size_t q = PI(e, p);
         int c = w.posc[p];
+        b.death_loc[q] = (int16_t)(keep_loc && c >= 0 ? T.c2f[c] : -1);
         if (c >= 0) {
             int f = T.c2f[c];
             d ^= zpiece(p, w.type[p], f);
@@ -568,7 +570,6 @@ __device__ int64_t warp_surrender(const jq_batch &b, const Topo &T, WEnv &w, int
         b.pos_y[q] = -1;
         b.death_reason[q] = DR_KBE;
         b.death_step[q] = (int16_t)step;
-        b.death_loc[q] = -1;
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) d ^= __shfl_xor_sync(FULL, d, o);
@@ -821,9 +822,13 @@ __device__ bool warp_step(const jq_batch &b, const Topo &T, WEnv &w, int e, int 
     if (lane == 0) {
         check_victory(w, x.acting, x.new_mc, x.new_mslc, x.term, x.win, x.draw);
         int cand = (x.acting + 1) & 3;
-        // plain moves test Q12 only past a dead next seat (batched_state.py:636-684)
-        x.do_q12 = x.combat ? !x.term : (int)w.sdead[cand];
-        x.new_turn = x.combat ? (x.term ? x.acting : (x.acting + 1) & 3) : cand;
+        // Batched rules: plain moves test Q12 only past a dead next seat
+        // (batched_state.py:636-684).  GameState rules and every combat ply:
+        // victory first, then Q12 on every candidate (batched_state.py:
+        // 905-918, state.py:595-612, 1111-1170).
+        x.full_advance = x.combat || b.rules == JQ_RULES_GAMESTATE;
+        x.do_q12 = x.full_advance ? !x.term : (int)w.sdead[cand];
+        x.new_turn = x.full_advance ? (x.term ? x.acting : (x.acting + 1) & 3) : cand;
     }
     __syncwarp();
     if (x.do_q12) {
@@ -838,7 +843,7 @@ __device__ bool warp_step(const jq_batch &b, const Topo &T, WEnv &w, int e, int 
             ++chain;
         }
         if (lane == 0) {
-            x.new_turn = x.combat ? (found ? cand : (x.acting + 1) & 3) : cand;
+            x.new_turn = x.full_advance ? (found ? cand : (x.acting + 1) & 3) : cand;
             check_victory(w, x.acting, x.new_mc, x.new_mslc, x.term, x.win, x.draw);
         }
     }

@@ -767,9 +767,11 @@ static int64_t flag_reveal_delta(jqo_batch *b, int e, int seat) {
     return 0;
 }
 
-/* batched_state.py:1078-1121 */
+/* batched_state.py:1078-1121 (death_loc -1); with GameState rules the
+ * current cell is kept as death_loc (state.py:640-693). */
 static int64_t surrender_delta(jqo_batch *b, int e, int seat, int step) {
     int64_t d = 0;
+    int keep_loc = b->rules == 1;
     b->seat_dead[SI(e, seat)] = 1;
     d ^= Z_sdead[seat];
     for (int p = 0; p < NP; ++p) {
@@ -786,7 +788,7 @@ static int64_t surrender_delta(jqo_batch *b, int e, int seat, int step) {
         b->pos_y[q] = -1;
         b->death_reason[q] = DR_KBE;
         b->death_step[q] = (int16_t)step;
-        b->death_loc[q] = -1;
+        b->death_loc[q] = (int16_t)(keep_loc && px >= 0 && py >= 0 ? py * 17 + px : -1);
     }
     return d;
 }
@@ -869,6 +871,8 @@ static void step_env(jqo_batch *b, int e, int32_t act, int mode, jqo_step_out *o
         b->pos_y[PI(e, A)] = (int8_t)(df / 17);
         b->move_count[PI(e, A)]++;
         new_mslc = mslc + 1;
+    }
+    if (D < 0 && b->rules != 1) {
         /* _advance_turn_vec (batched_state.py:615-686): Q12 only past a dead seat */
         int cand = (acting + 1) % 4;
         if (b->seat_dead[SI(e, cand)]) {
@@ -886,8 +890,10 @@ static void step_env(jqo_batch *b, int e, int32_t act, int mode, jqo_step_out *o
         new_turn = cand;
         check_victory(b, e, acting, new_mc, new_mslc, &term, &win, &draw);
     } else {
-        /* combat path (_step_single) */
+        /* combat path (_step_single); plain moves too under GameState rules
+           (state.py:309-669 runs the same sequence for every ply) */
         int death_step = mc + 1;
+      if (D >= 0) {
         int fr_src = (A_type == T_SILING) && (ev == EV_KILLED || ev == EV_BOMB);
         int fr_dst = (D_type == T_SILING) && (ev == EV_EAT || ev == EV_BOMB);
         if (fr_src) zob ^= flag_reveal_delta(b, e, A_seat);
@@ -917,6 +923,7 @@ static void step_env(jqo_batch *b, int e, int32_t act, int mode, jqo_step_out *o
             kill_piece(b, e, D, df, DR_MUTUAL, death_step, df);
         }
         new_mslc = 0;
+      }
         if (fcap && !b->seat_dead[SI(e, D_seat)]) {
             zob ^= flag_reveal_delta(b, e, D_seat);
             zob ^= surrender_delta(b, e, D_seat, death_step);

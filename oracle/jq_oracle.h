@@ -69,6 +69,7 @@ typedef struct {
     uint8_t *bel_code;
     int16_t *remaining;
     uint8_t *rem_tracked;
+    int32_t rules; /* 0: BatchedGameState rules, 1: GameState rules */
 } jqo_batch;
 
 /* Per-step outputs (n,) */

@@ -94,7 +94,7 @@ _CTYPE = {
 class _CBatch(ctypes.Structure):
     _fields_ = [("n", ctypes.c_int32)] + [
         (name, ctypes.POINTER(_CTYPE[dt])) for name, dt, _, _ in FIELDS
-    ]
+    ] + [("rules", ctypes.c_int32)]
 
 
 class _CStepOut(ctypes.Structure):
@@ -231,14 +231,17 @@ def topology() -> dict[str, np.ndarray]:
 class OracleBatch:
     """N environments in the device's field-major layout, stepped on the CPU."""
 
-    def __init__(self, n: int, show_mode: int = 2):
+    def __init__(self, n: int, show_mode: int = 2, rules: int = 0):
+        """rules: 0 = BatchedGameState rules, 1 = GameState rules (state.py)."""
         self.n = int(n)
         self.show_mode = int(show_mode)
+        self.rules = int(rules)
         self.a: dict[str, np.ndarray] = {}
         for name, dt, shape, fill in FIELDS:
             self.a[name] = np.full((self.n,) + shape, fill, dtype=dt)
         self._c = _CBatch()
         self._c.n = self.n
+        self._c.rules = self.rules
         for name, dt, _, _ in FIELDS:
             setattr(self._c, name, _ptr(self.a[name], _CTYPE[dt]))
         self.threads = int(os.environ.get("JQ_ORACLE_THREADS", "1"))

@@ -3,7 +3,7 @@
 A driver adapts an implementation (the CPU oracle, or the CUDA batch through
 the C-ABI) to five calls:
 
-    load(init: dict[str, ndarray], show_mode)   # oracle field names
+    load(init: dict[str, ndarray], show_mode, rules)   # oracle field names
     legal() -> (offsets, values)                 # CSR for the current turns
     masks() -> (N, 16641) bool                   # canonical masks, current turns
     step(actions) -> dict                        # MoveResultBatch arrays
@@ -23,7 +23,9 @@ from pathlib import Path
 import numpy as np
 
 GOLDEN = Path(__file__).resolve().parent / "golden"
-TRAJECTORIES = ("cfg1", "combat_dark", "long_bright", "late_game")
+# batched trajectories (BatchedGameState.step_batch) and GameState trajectories
+# (GameState.step, the single-env rules); the latter carry ``rules == 1``
+TRAJECTORIES = ("cfg1", "combat_dark", "long_bright", "late_game", "gs_uniform", "gs_combat_dark", "gs_late")
 
 CM_ORDER = ["cm_direct_lo", "cm_direct_hi", "cm_direct_type", "cm_last_direct_step",
             "cm_direct_other", "cm_chain_lo", "cm_chain_hi", "cm_chain_type",
@@ -69,7 +71,7 @@ def replay(fx: dict, drv, plies: int | None = None, check_obs: bool = True,
            check_every_cm: bool = True) -> int:
     """Replay ``fx`` through ``drv``; returns the number of plies checked."""
     T = fx["actions"].shape[0] if plies is None else min(plies, fx["actions"].shape[0])
-    drv.load(init_state(fx), int(fx["show_mode"]))
+    drv.load(init_state(fx), int(fx["show_mode"]), int(fx["rules"]) if "rules" in fx else 0)
     obs_at: dict[int, list] = {}
     for (t, e, s), h in zip(fx["obs_keys"].tolist(), fx["obs_sha"].tolist()):
         obs_at.setdefault(int(t), []).append((int(e), int(s), h))

@@ -14,6 +14,10 @@ What is recorded (all produced by junqi_core itself):
   digests of the ten Zobrist tables (``_zobrist.py``), and the first 64
   entries of the default setup pool (``gpu_rollout._build_setup_pool``) plus
   32 ``generate_random_setup(random.Random(s))`` lineups.
+* ``ref_traj_gs_<name>.npz`` -- the same records for trajectories stepped
+  with ``GameState.step`` (state.py, the single-env rules JunqiEnv uses),
+  beliefs from ``BeliefTensor.update`` on those states and observations
+  from ``ObservationBuilder`` -- exactly the JunqiEnv path.
 * ``ref_traj_<name>.npz`` -- a batched trajectory through
   ``BatchedGameState.step_batch`` (the state contract): initial state, the
   action stream, per-ply Zobrist hashes and MoveResultBatch arrays,
@@ -240,6 +244,115 @@ def record(name: str, b: BatchedGameState, plies: int, policy, show_mode: ShowMo
     return stats
 
 
+# ---------------------------------------------------------------------------
+# GameState trajectories (the single-env rules JunqiEnv steps, state.py)
+# ---------------------------------------------------------------------------
+_GS_FIELDS = [("alive", "alive"), ("piece_type_arr", "piece_type"), ("piece_seat_arr", "piece_seat"),
+              ("pos_x", "pos_x"), ("pos_y", "pos_y"), ("zero_x", "zero_x"), ("zero_y", "zero_y"),
+              ("move_count_arr", "move_count"), ("active_eat_arr", "active_eat"),
+              ("passive_surv_arr", "passive_surv"), ("death_reason_arr", "death_reason"),
+              ("death_step_arr", "death_step"), ("death_loc_flat_arr", "death_loc"),
+              ("cell_piece_id", "cell_pid"), ("seat_dead_arr", "seat_dead"),
+              ("seat_flag_revealed_arr", "seat_flag")]
+_CM_MINE = {"cm_direct_lo": "cm_direct_lo", "cm_direct_hi": "cm_direct_hi", "cm_direct_type": "cm_direct_type",
+            "cm_last_direct_step": "cm_last_direct_step", "cm_direct_other_count": "cm_direct_other",
+            "cm_chain_lo": "cm_chain_lo", "cm_chain_hi": "cm_chain_hi", "cm_chain_type": "cm_chain_type",
+            "cm_last_chain_step": "cm_last_chain_step", "cm_eaten_by_pid_lo": "cm_eaten_lo",
+            "cm_eaten_by_pid_hi": "cm_eaten_hi", "cm_rank_floor": "cm_rank_floor",
+            "cm_rank_floor_step": "cm_rank_floor_step", "cm_is_gongb": "cm_is_gongb",
+            "cm_not_gongb": "cm_not_gongb", "cm_attacked_by_known_gongb": "cm_atk_gongb"}
+
+
+def gs_state(games: list) -> dict[str, np.ndarray]:
+    out = {mine: np.stack([np.asarray(getattr(g, ref)) for g in games]) for ref, mine in _GS_FIELDS}
+    out["turn"] = np.array([g.turn.value for g in games], np.int8)
+    out["zobrist"] = np.array([np.int64(np.uint64(g.zobrist & (2**64 - 1)).astype(np.int64)) for g in games], np.int64)
+    out["move_counter"] = np.array([g.move_counter for g in games], np.int32)
+    out["mslc"] = np.array([g.moves_since_last_combat for g in games], np.int32)
+    out["terminated"] = np.array([g.terminated for g in games], bool)
+    out["winner"] = np.array([-1 if g.winner_team is None else g.winner_team for g in games], np.int8)
+    out["draw"] = np.array([g.draw for g in games], bool)
+    for ref_field, (batched_name, _) in zip([f for _, f in CM_FIELDS], CM_FIELDS):
+        out[_CM_MINE[batched_name]] = np.stack([np.asarray(getattr(g.combat_memory, ref_field)) for g in games])
+    return out
+
+
+def record_gamestate(name: str, games: list, plies: int, seed: int, combat_bias: bool, show_mode: ShowMode,
+                     obs_plies: tuple[int, ...], obs_envs: int) -> dict:
+    from junqi_core.state import Action
+    rng = random.Random(seed)
+    N = len(games)
+    init = gs_state(games)
+    beliefs = [[BeliefTensor.initial(g, Seat(s)) for s in range(4)] for g in games]
+    builder = ObservationBuilder()
+    sp = np.zeros((317, 17, 17), np.float32)
+    gl = np.zeros(28, np.float32)
+    acts_all = np.zeros((plies, N), np.int32)
+    zob = np.zeros((plies, N), np.int64)
+    res = {k: np.zeros((plies, N), np.int8) for k in ("valid", "event", "terminated", "winner", "draw", "flag")}
+    csr_sha, mask_sha, cm_sha, obs_keys, obs_sha = [], [], [], [], []
+    cm_order = [_CM_MINE[b] for b, _ in CM_FIELDS]
+
+    def snap(t):
+        for i in range(min(obs_envs, N)):
+            for s in range(4):
+                builder.build_into(games[i], beliefs[i][s], Seat(s), sp, gl)
+                obs_keys.append((t, i, s))
+                obs_sha.append(sha(sp, gl))
+
+    for t in range(plies):
+        if t in obs_plies:
+            snap(t)
+        ids = [g.legal_action_ids() for g in games]
+        offsets = np.zeros(N + 1, np.int32)
+        np.cumsum([len(x) for x in ids], out=offsets[1:])
+        values = np.concatenate(ids).astype(np.int32) if any(len(x) for x in ids) else np.zeros(0, np.int32)
+        csr_sha.append(sha(offsets, values))
+        mask_sha.append(sha(np.stack([canonical_mask(np.asarray(ids[i]), games[i].turn.value) for i in range(N)])))
+        for i, g in enumerate(games):
+            w = -1 if g.winner_team is None else g.winner_team
+            if g.terminated or len(ids[i]) == 0:
+                res["terminated"][t, i], res["winner"][t, i], res["draw"][t, i] = g.terminated, w, g.draw
+                continue
+            pool = ids[i]
+            if combat_bias:
+                occ = g.cell_piece_id[np.asarray(pool) % 289] >= 0
+                if occ.any():
+                    pool = np.asarray(pool)[occ]
+            a = int(rng.choice(list(pool)))
+            acts_all[t, i] = a
+            sf, df = a // 289, a % 289
+            new, mr = g.step(Action(seat=g.turn, src=(sf % 17, sf // 17), dst=(df % 17, df // 17)))
+            for s in range(4):
+                beliefs[i][s].update(g, new, mr)
+            games[i] = new
+            res["valid"][t, i] = 1
+            res["event"][t, i] = mr.event.value
+            res["terminated"][t, i] = new.terminated
+            res["winner"][t, i] = -1 if new.winner_team is None else new.winner_team
+            res["draw"][t, i] = new.draw
+            res["flag"][t, i] = mr.flag_captured
+        st = gs_state(games)
+        zob[t] = st["zobrist"]
+        cm_sha.append(sha(*[st[k] for k in cm_order]))
+    if plies in obs_plies:
+        snap(plies)
+    events = res["event"][res["valid"] == 1]
+    stats = {"plies": plies, "envs": N, "valid_steps": int((res["valid"] == 1).sum()),
+             "eat": int((events == 2).sum()), "bomb": int((events == 3).sum()), "killed": int((events == 4).sum()),
+             "flag_captured": int(res["flag"].sum()), "terminated_final": int(sum(g.terminated for g in games)),
+             "seat_deaths": int(sum(int(np.asarray(g.seat_dead_arr).sum()) for g in games))}
+    out = {f"init_{k}": v for k, v in init.items()}
+    out.update({f"final_{k}": v for k, v in gs_state(games).items()})
+    out.update({"actions": acts_all, "zobrist": zob, **{f"res_{k}": v for k, v in res.items()},
+                "csr_sha": np.array(csr_sha), "mask_sha": np.array(mask_sha), "cm_sha": np.array(cm_sha),
+                "obs_keys": np.array(obs_keys, np.int32).reshape(-1, 3), "obs_sha": np.array(obs_sha),
+                "show_mode": np.int32(show_mode.value), "rules": np.int32(1)})
+    np.savez_compressed(OUT / f"ref_traj_{name}.npz", **out)
+    print(name, stats, flush=True)
+    return stats
+
+
 def uniform_policy(seed: int):
     rng = random.Random(seed)
 
@@ -339,6 +452,16 @@ def main() -> None:
     b = BatchedGameState.from_game_states(late_game_states(32, 5, ShowMode.HALF_DARK))
     manifest["trajectories"]["late_game"] = record(
         "late_game", b, 600, uniform_policy(17), ShowMode.HALF_DARK, obs_plies=(0, 300, 600), obs_envs=8)
+    games = [GameState.new_game(generate_random_setup(random.Random(4000 + i))) for i in range(48)]
+    manifest["trajectories"]["gs_uniform"] = record_gamestate(
+        "gs_uniform", games, 400, 21, False, ShowMode.HALF_DARK, obs_plies=(0, 200, 400), obs_envs=8)
+    games = [GameState.new_game(generate_random_setup(random.Random(5000 + i)), show_mode=ShowMode.DARK)
+             for i in range(32)]
+    manifest["trajectories"]["gs_combat_dark"] = record_gamestate(
+        "gs_combat_dark", games, 500, 23, True, ShowMode.DARK, obs_plies=(250, 500), obs_envs=8)
+    games = late_game_states(32, 6, ShowMode.HALF_DARK)
+    manifest["trajectories"]["gs_late"] = record_gamestate(
+        "gs_late", games, 500, 29, True, ShowMode.HALF_DARK, obs_plies=(0, 250, 500), obs_envs=8)
     (OUT / "ref_manifest.json").write_text(json.dumps(manifest, indent=1, sort_keys=True))
 
 

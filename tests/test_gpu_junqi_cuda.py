@@ -1,0 +1,126 @@
+"""The reference-compatible ``junqi_cuda`` surface (junqi_b200.junqi_cuda).
+
+Drives the module the way the reference's own GPU parity tests drive the
+original extension (tests/test_gpu_step_batch.py, test_gpu_csr_mask.py,
+test_gpu_obs_parity.py in freezeng123456/JunQi): upload a batch through
+``copy_from_host`` with the reference's dictionary keys, step it with
+``step_batch``, query legal actions in the dense / CSR / canonical-mask
+forms, build observations, reset from an uploaded pool -- and compare with
+the CPU oracle at every step.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from junqi_b200 import junqi_cuda as jc
+from junqi_b200 import tables
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+REF_KEYS = {"piece_seat_arr": "piece_seat", "piece_type_arr": "piece_type", "alive": "alive", "pos_x": "pos_x",
+            "pos_y": "pos_y", "zero_x": "zero_x", "zero_y": "zero_y", "move_count_arr": "move_count",
+            "active_eat_arr": "active_eat", "passive_surv_arr": "passive_surv", "death_reason_arr": "death_reason",
+            "death_step_arr": "death_step", "death_loc_flat_arr": "death_loc", "cell_piece_id": "cell_pid",
+            "seat_dead_arr": "seat_dead", "seat_flag_revealed_arr": "seat_flag", "turn": "turn",
+            "zobrist": "zobrist", "move_counter": "move_counter", "moves_since_last_combat": "mslc"}
+
+
+def _setup():
+    jc.set_device(0)
+    jc.init_tables()
+    z = tables.zobrist_tables()
+    jc.upload_zobrist_tables(z["piece"].ravel(), z["turn"], z["move_counter"], z["mslc"], z["winner"],
+                             int(z["terminated"][0]), int(z["draw"][0]), z["seat_dead"], z["seat_flag"])
+
+
+def _pack(orc: O.OracleBatch) -> dict:
+    d = {ref: orc.a[m].reshape(-1).copy() for ref, m in REF_KEYS.items()}
+    for k in ("alive", "seat_dead_arr", "seat_flag_revealed_arr"):
+        d[k] = d[k].astype(bool)
+    return d
+
+
+def test_step_batch_and_legal_forms_match_oracle():
+    _setup()
+    n = 24
+    pool = tables.build_setup_pool(n, seed=31)
+    orc = O.OracleBatch(n, 2)
+    for e in range(n):
+        orc.reset_env(e, pool[e])
+    state = jc.DeviceGameStateBatch(n)
+    state.copy_from_host(_pack(orc))
+    state.copy_termination_from_host(np.zeros(n, bool), np.full(n, -1, np.int8), np.zeros(n, bool))
+    rng = np.random.default_rng(4)
+    for step in range(120):
+        turn = state.copy_turn_to_host()
+        assert np.array_equal(turn, orc["turn"])
+        ids, counts = jc.legal_action_ids_batch(state, turn)
+        off, val = jc.legal_action_ids_batch_csr(state, turn)
+        o_off, o_val = orc.legal()
+        assert np.array_equal(off, o_off) and np.array_equal(val, o_val), f"CSR differs at step {step}"
+        for e in range(n):
+            assert np.array_equal(ids[e, :counts[e]], o_val[o_off[e]:o_off[e + 1]])
+        ptr = jc.legal_mask_canonical_batch(state, turn)
+        mask = state._mask.cpu().numpy().astype(bool)
+        assert ptr == state._mask.data_ptr()
+        for e in range(0, n, 5):
+            assert np.array_equal(mask[e], orc.canonical_mask(o_val[o_off[e]:o_off[e + 1]], int(turn[e])))
+        acts = np.array([val[off[e] + rng.integers(counts[e])] if counts[e] else 0 for e in range(n)], np.int32)
+        r = state.step_batch(acts)
+        ro = orc.step(acts)
+        for k, ok in (("valid", "valid"), ("event", "event"), ("terminated", "terminated"),
+                      ("winner_team", "winner"), ("draw", "draw"), ("flag_captured", "flag_captured")):
+            assert np.array_equal(np.asarray(r[k]).astype(np.int64), ro[ok].astype(np.int64)), (step, k)
+        h = state.copy_to_host()
+        for ref, m in REF_KEYS.items():
+            assert np.array_equal(np.asarray(h[ref]).astype(np.int64).reshape(-1),
+                                  orc.a[m].astype(np.int64).reshape(-1)), (step, ref)
+    cm = state.cm_copy_to_host()
+    assert np.array_equal(cm["chain_lo"], orc["cm_chain_lo"].reshape(-1))
+    assert np.array_equal(cm["rank_floor"], orc["cm_rank_floor"].reshape(-1))
+
+
+def test_reset_pool_and_single_seat_observation_match_oracle():
+    _setup()
+    n = 16
+    pool = tables.build_setup_pool(40, seed=12)
+    jc.upload_setup_pool(pool)
+    state = jc.DeviceGameStateBatch(n)
+    state.copy_termination_from_host(np.ones(n, bool), np.full(n, -1, np.int8), np.zeros(n, bool))
+    jc.reset_terminated_envs(state, 99)
+    from junqi_b200 import _native as N
+    orc = O.OracleBatch(n, 2)
+    for e in range(n):
+        orc.reset_env(e, pool[N.lib().jq_pool_index(99, 1, e, pool.shape[0])])
+    h = state.copy_to_host()
+    assert np.array_equal(h["zobrist"], orc["zobrist"])
+    obs = jc.DeviceObservationSingleBatch(n)
+    seats = torch.from_numpy(orc["turn"].copy()).cuda()
+    jc.build_observation_single_seat(state, obs, seats.data_ptr(), 2)
+    sp, gl = obs.copy_to_host()
+    osp, ogl = orc.obs()
+    assert np.array_equal(sp, osp) and np.array_equal(gl, ogl)
+    obs4 = jc.DeviceObservationBatch(n)
+    jc.build_observation_batch(state, np.zeros((n, 4, 12, 289), np.float32),
+                               np.tile(np.arange(4, dtype=np.int8), (n, 1)), obs4, 2)
+    sp4, _ = obs4.copy_to_host()
+    for s in range(4):
+        o_sp, _ = orc.obs(np.full(n, s, np.int8))
+        assert np.array_equal(sp4[:, s], o_sp)
+
+
+def test_step_device_pointer_dict():
+    _setup()
+    n = 8
+    state = jc.DeviceGameStateBatch(n)
+    jc.upload_setup_pool(tables.build_setup_pool(8, seed=2))
+    state.copy_termination_from_host(np.ones(n, bool), np.full(n, -1, np.int8), np.zeros(n, bool))
+    jc.reset_terminated_envs(state, 5)
+    turn = torch.zeros(n, dtype=torch.int8, device="cuda")
+    acts = torch.full((n,), -1, dtype=torch.int32, device="cuda")
+    d = jc.step_device(state, acts.data_ptr(), turn.data_ptr())
+    assert d["N"] == n and all(isinstance(v, int) for v in d.values())
+    assert not state._out["valid"].any()

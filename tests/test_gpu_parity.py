@@ -1,12 +1,13 @@
 """GPU parity: the CUDA path through the C ABI against the reference.
 
-1. The four reference golden trajectories (junqi_core output recorded in
-   tests/golden) replayed through jq_step / jq_legal / jq_csr / jq_observe:
+1. The reference golden trajectories (junqi_core output recorded in
+   tests/golden; four stepped by BatchedGameState, three by GameState) replayed through jq_step / jq_legal / jq_csr / jq_observe:
    every legal CSR, canonical mask, MoveResult, Zobrist, combat-memory
    digest, observation digest and the final SoA state must match bit for bit.
 2. Long seeded rollouts through the fused ply kernel with auto-reset from a
    setup pool, checked against the CPU oracle after every ply (state,
-   MoveResult, CSR, masks, observations), in all three show modes.
+   MoveResult, CSR, masks, observations), in all three show modes and under
+   both rule sets.
 All comparisons are exact (integer / byte work, float32 values compared by
 bit pattern).
 """
@@ -28,9 +29,9 @@ pytestmark = pytest.mark.gpu
 
 
 class CudaDriver:
-    def load(self, init, show_mode):
+    def load(self, init, show_mode, rules):
         n = init["turn"].shape[0]
-        self.env = JunqiEnvB200(n, show_mode=show_mode, pool_size=4, obs_seats=4)
+        self.env = JunqiEnvB200(n, show_mode=show_mode, pool_size=4, obs_seats=4, rules=rules)
         self.env.load_state(init)
         self.ver, self.obs_ver, self.obs_cache = 0, -1, None
 
@@ -112,17 +113,19 @@ def _compare_obs(env, orc, t, seats):
     assert np.array_equal(gl.view(np.uint32), ogl.view(np.uint32)), f"ply {t}: global features differ"
 
 
-@pytest.mark.parametrize("mode,n,plies,policy", [
-    (HALF_DARK, 256, 400, "uniform"),
-    (DARK, 128, 300, "softmax"),
-    (BRIGHT, 128, 300, "uniform"),
+@pytest.mark.parametrize("mode,n,plies,policy,rules", [
+    (HALF_DARK, 256, 400, "uniform", N.RULES_BATCHED),
+    (DARK, 128, 300, "softmax", N.RULES_BATCHED),
+    (BRIGHT, 128, 300, "uniform", N.RULES_BATCHED),
+    (HALF_DARK, 256, 600, "softmax", N.RULES_GAMESTATE),
+    (DARK, 128, 500, "uniform", N.RULES_GAMESTATE),
 ])
-def test_rollout_with_autoreset_matches_oracle(mode, n, plies, policy):
+def test_rollout_with_autoreset_matches_oracle(mode, n, plies, policy, rules):
     pool = tables.build_setup_pool(257, seed=5)
     L = N.lib()
-    env = JunqiEnvB200(n, show_mode=mode, pool=pool, obs_seats=1)
-    orc = O.OracleBatch(n, mode)
-    seed = 1234 + mode
+    env = JunqiEnvB200(n, show_mode=mode, pool=pool, obs_seats=1, rules=rules)
+    orc = O.OracleBatch(n, mode, rules=rules)
+    seed = 1234 + mode + 17 * rules
     env.reset(seed=seed, ply=0, all_envs=True)
     for e in range(n):
         orc.reset_env(e, pool[L.jq_pool_index(seed, 0, e, pool.shape[0])])

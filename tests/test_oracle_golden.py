@@ -14,9 +14,9 @@ from tests import _golden as G
 
 
 class OracleDriver:
-    def load(self, init, show_mode):
+    def load(self, init, show_mode, rules):
         n = init["turn"].shape[0]
-        self.b = O.OracleBatch(n, show_mode)
+        self.b = O.OracleBatch(n, show_mode, rules=rules)
         O.load_state(self.b, init)
 
     def legal(self):
