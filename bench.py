@@ -63,6 +63,17 @@ def obs_read_bytes() -> int:
     return piece + cm_obs + cm_opp + other
 
 
+def pipeline_roofline(plies_per_gpu: float, seats: int, k_avg: float, peak: float) -> dict:
+    """Whole step + mask + obs pipeline against HBM: the compulsory bytes of
+    one env-ply of the API tensors (obs written, canonical mask written, CSR
+    written, game SoA read + written, combat memory read, the observer's
+    belief slice read, the action read) times plies/s per GPU."""
+    b_ply = seats * (OBS_WRITE + 13_872) + 16_641 + 4 * (k_avg + 1) + 2 * 3_142 + 30_720 + 4
+    achieved = plies_per_gpu * b_ply / 1e9
+    return {"bytes_per_ply": b_ply, "legal_per_env": k_avg, "achieved": achieved, "unit": "GB/s per GPU",
+            "peak": peak, "frac": achieved / peak}
+
+
 def sample_clocks(dev: int, stop: threading.Event, rows: list) -> None:
     q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -233,12 +244,13 @@ def main() -> None:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
 
     from junqi_b200 import _native
+    from junqi_b200 import sharding
     from junqi_b200 import tables
     from junqi_b200.env import JunqiEnvB200
     _native.build()
 
     n, seats = cfg["envs"], cfg["seats"]
-    seed = args.seed + rank * 10_000
+    seed = sharding.rank_seed(args.seed, rank)
     pool = tables.build_setup_pool(cfg["pool"], seed=42)
     env = JunqiEnvB200(n, device=local, show_mode=cfg["mode"], pool=pool, obs_seats=seats,
                        rules=RULES[args.rules])
@@ -280,7 +292,7 @@ def main() -> None:
         t = args.warmup + 1 + k
         applied += one_ply(t, evs[k])
     if world > 1:
-        dist.all_reduce(env.stats)  # one collective per rollout: episode statistics
+        sharding.reduce_episode_stats(env.stats)  # one collective per rollout: episode statistics
     end.record(stream)
     torch.cuda.synchronize()
     t_wall = time.perf_counter() - t_wall
@@ -292,14 +304,11 @@ def main() -> None:
     obs_ms = [e[0].elapsed_time(e[1]) for e in evs]
     ply_ms = [e[2].elapsed_time(e[3]) for e in evs]
     plies_local = int(applied.sum(dtype=torch.int64).item())
-    t_max = torch.tensor([ms_total], dtype=torch.float64, device=env.device)
-    tot = torch.tensor([plies_local], dtype=torch.int64, device=env.device)
-    if world > 1:
-        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
-        dist.all_reduce(tot)
-    ms_max = float(t_max.item())
-    plies_all = int(tot.item())
+    ms_max = sharding.max_over_ranks(ms_total, env.device)
+    plies_all = sharding.sum_over_ranks(plies_local, env.device)
     value = plies_all / (ms_max / 1e3)
+
+    k_avg = float(env.counts.sum(dtype=torch.int64).item()) / n  # legal actions per env, last ply
 
     # e2e through the public API with host buffers: H2D actions, D2H results + CSR, host policy
     e2e = None
@@ -329,6 +338,7 @@ def main() -> None:
                          "traffic": None if traffic_unit is None else traffic_unit * units,
                          "algorithmic_bytes_per_launch": obs_bytes, "avg_launch_ms": obs_avg,
                          "ply_kernel_avg_ms": statistics.mean(ply_ms)},
+            "pipeline": pipeline_roofline(value / world, seats, k_avg, peak),
             "clocks": summarize_clocks(clock_rows),
             "gpu_launches": 3 * args.steps,  # obs_kernel + sample kernel + rules_kernel per ply
             "episode_stats": {"wins_team0": stats[0], "wins_team1": stats[1], "draws": stats[2],

@@ -53,7 +53,9 @@ enum { JQ_BRIGHT = 0, JQ_DARK = 1, JQ_HALF_DARK = 2 };
 
 /*
  * Batch of N envs.  Shapes are per env; every array is contiguous with the
- * env index outermost.  Replaces DeviceGameStateBatch (junqi_cuda.h:48-111)
+ * env index outermost and aligned to its element size; bel_code must be
+ * 16-byte aligned (the kernels move it in 16-byte words).  Entry points
+ * taking a batch return JQ_ERR_ARG otherwise.  Replaces DeviceGameStateBatch (junqi_cuda.h:48-111)
  * plus the CombatMemory, move-history and belief buffers the reference keeps
  * in process-global scratch.
  */
@@ -160,6 +162,12 @@ int jq_reset(const jq_batch *b, uint64_t seed, uint64_t ply, int32_t all, int32_
  * (bindings.cpp:1262-1270). */
 int jq_init_beliefs(const jq_batch *b, int32_t show_mode, void *stream);
 
+/* Rebuild every env's Zobrist hash from its state, for state written by the
+ * caller (a position built on the host).  Device counterpart of the
+ * reference's host-side _recompute_zobrist (state.py:1761-1815), which
+ * GameState.from_dict uses; bindings.cpp has no such entry point. */
+int jq_rehash(const jq_batch *b, int32_t show_mode, void *stream);
+
 /* One ply for every env: world action id src_flat*289+dst_flat per env.
  * BatchedGameState.step_batch semantics, plus combat memory, beliefs, move
  * history and terminal reward.  Replaces DeviceGameStateBatch.step_batch /
@@ -220,7 +228,9 @@ int jq_csr_noalloc(int32_t n, const int32_t *d_counts, const int32_t *d_ids, int
  * (N*seats, 317, 17, 17) float32 and d_global (N*seats, 28) float32.
  * ObservationBuilder._fill_into semantics (observation.py:598-858).
  * Replaces build_observation_batch(_resident) / build_observation_single_seat
- * (bindings.cpp:803-829, 1091-1182). */
+ * (bindings.cpp:803-829, 1091-1182).  Units are scheduled through one of 256
+ * device-side tickets per GPU, taken in call order: at most 256 calls may be
+ * in flight on one GPU at a time (across all streams). */
 int jq_observe(const jq_batch *b, const int8_t *d_observers, int32_t seats_per_env,
                int32_t show_mode, float *d_spatial, float *d_global, void *stream);
 

@@ -79,6 +79,18 @@ class DeviceBatch:
     def struct(self) -> N.JqBatch:
         return self._struct
 
+    def view(self, start: int, count: int) -> N.JqBatch:
+        """jq_batch describing envs [start, start + count) of this batch (no copy)."""
+        if not (0 <= start and count > 0 and start + count <= self.n):
+            raise ValueError(f"env range [{start}, {start + count}) outside [0, {self.n})")
+        s = N.JqBatch()
+        s.n = int(count)
+        s.rules = self._struct.rules
+        for name, _, _, _ in FIELDS:
+            t = self.t[name]
+            setattr(s, name, t.data_ptr() + start * t.stride(0) * t.element_size())
+        return s
+
     def __getitem__(self, k: str) -> torch.Tensor:
         return self.t[k]
 
@@ -92,11 +104,14 @@ class DeviceBatch:
                 a = a.view(_SIGNED_VIEW[dt])
             self.t[name].copy_(torch.from_numpy(a))
 
-    def to_host(self, names=None) -> dict[str, np.ndarray]:
+    def to_host(self, names=None, envs=None) -> dict[str, np.ndarray]:
+        """Host copies of the fields (all, or `names`), for all envs or the index list `envs`."""
+        idx = None if envs is None else torch.as_tensor(np.asarray(envs, np.int64), device=self.device)
         out = {}
         for name, dt, _, _ in FIELDS:
             if names is not None and name not in names:
                 continue
-            a = self.t[name].cpu().numpy()
+            t = self.t[name] if idx is None else self.t[name].index_select(0, idx)
+            a = t.cpu().numpy()
             out[name] = a.view(dt) if dt in _SIGNED_VIEW else a.astype(dt, copy=False)
         return out

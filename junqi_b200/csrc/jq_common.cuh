@@ -87,5 +87,16 @@ __host__ __device__ inline uint64_t hash3(uint64_t a, uint64_t b, uint64_t c) {
 
 __device__ __forceinline__ bool mbit(const uint32_t *m, int c) { return (m[c >> 5] >> (c & 31)) & 1u; }
 __device__ __forceinline__ void mset(uint32_t *m, int c) { m[c >> 5] |= 1u << (c & 31); }
+// The same on a 5-word mask held in registers: select instead of a dynamic
+// index, so the array stays in registers rather than local memory.
+__device__ __forceinline__ bool rbit(const uint32_t (&m)[5], int c) {
+    const uint32_t wd = c < 64 ? (c < 32 ? m[0] : m[1]) : (c < 96 ? m[2] : (c < 128 ? m[3] : m[4]));
+    return (wd >> (c & 31)) & 1u;
+}
+__device__ __forceinline__ void rset(uint32_t (&m)[5], int c) {
+    const uint32_t bit = 1u << (c & 31), wi = (uint32_t)c >> 5;
+#pragma unroll
+    for (uint32_t i = 0; i < 5; ++i) m[i] |= wi == i ? bit : 0u;
+}
 
 }  // namespace jq

@@ -8,6 +8,7 @@
 // caller's stream.
 #include <cstdio>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 
 #include "jq_obs.cuh"
@@ -46,14 +47,14 @@ __device__ __forceinline__ int pool_index(uint64_t seed, uint64_t ply, int e, in
     return (int)(hash3(seed, ply, (uint64_t)e) % (uint64_t)P);
 }
 
-__global__ void __launch_bounds__(RULE_THREADS) rules_kernel(RuleArgs a) {
+__global__ void __launch_bounds__(RULE_THREADS, 4) rules_kernel(RuleArgs a) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     RuleSmem &S = *reinterpret_cast<RuleSmem *>(smem_raw);
     {
-        const uint4 *src = reinterpret_cast<const uint4 *>(&c_topo);
+        const uint4 *src = reinterpret_cast<const uint4 *>(&g_topo);
         uint4 *dst = reinterpret_cast<uint4 *>(&S.topo);
         for (int k = threadIdx.x; k < (int)(sizeof(Topo) / 16); k += RULE_THREADS) dst[k] = src[k];
-        const unsigned char *s8 = reinterpret_cast<const unsigned char *>(&c_topo);
+        const unsigned char *s8 = reinterpret_cast<const unsigned char *>(&g_topo);
         unsigned char *d8 = reinterpret_cast<unsigned char *>(&S.topo);
         for (int k = (int)(sizeof(Topo) / 16) * 16 + threadIdx.x; k < (int)sizeof(Topo); k += RULE_THREADS)
             d8[k] = s8[k];
@@ -93,6 +94,34 @@ __global__ void __launch_bounds__(RULE_THREADS) rules_kernel(RuleArgs a) {
     }
 }
 
+// Zobrist hash of every env rebuilt from scratch (state.py:1761-1815), one
+// warp per env.
+__global__ void rehash_kernel(jq_batch b, int mode) {
+    const int lane = threadIdx.x & 31;
+    const int e = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (e >= b.n) return;
+    int64_t h = 0;
+    for (int p = lane; p < NP; p += 32) {
+        const size_t q = PI(e, p);
+        const int t = b.piece_type[q], x = b.pos_x[q], y = b.pos_y[q];
+        if (b.alive[q] && t >= 0 && x >= 0 && x < 17 && y >= 0 && y < 17) h ^= zpiece(p, t, y * 17 + x);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) h ^= __shfl_xor_sync(FULL, h, o);
+    if (lane == 0) {
+        const int w = b.winner[e];
+        h ^= c_zturn[b.turn[e] & 3] ^ g_zmc[b.move_counter[e] & 0xFFF] ^ g_zmslc[b.mslc[e] & 0x1FF];
+        h ^= c_zwin[(w == 0 || w == 1) ? w + 1 : 0] ^ c_zshow[mode & 3];
+        if (b.terminated[e]) h ^= c_zterm;
+        if (b.draw[e]) h ^= c_zdraw;
+        for (int s = 0; s < 4; ++s) {
+            if (b.seat_dead[(size_t)e * 4 + s]) h ^= c_zsdead[s];
+            if (b.seat_flag[(size_t)e * 4 + s]) h ^= c_zsflag[s];
+        }
+        b.zobrist[e] = h;
+    }
+}
+
 // compact canonical action -> world flat action (game_state.cu:2639-2685 semantics)
 __global__ void rotate_actions_kernel(int n, const int32_t *can, const int8_t *seats, const int8_t *turn,
                                       int32_t *world) {
@@ -105,11 +134,11 @@ __global__ void rotate_actions_kernel(int n, const int32_t *can, const int8_t *s
     // canonical -> world: invert the per-seat rotation by search over the 129 cells
     int ws = -1, wd = -1;
     for (int c = 0; c < NB; ++c) {
-        int r = c_topo.rot[seat][c];
+        int r = g_topo.rot[seat][c];
         if (r == cs) ws = c;
         if (r == cd) wd = c;
     }
-    world[e] = (ws < 0 || wd < 0) ? -1 : c_topo.c2f[ws] * NC + c_topo.c2f[wd];
+    world[e] = (ws < 0 || wd < 0) ? -1 : g_topo.c2f[ws] * NC + g_topo.c2f[wd];
 }
 
 // ---------------------------------------------------------------------------
@@ -199,9 +228,9 @@ __global__ void sample_softmax_kernel(int n, const int8_t *turn, const int32_t *
     int best_w = -1, best_c = -1;
     for (int j = 0; j < c; ++j) {
         int id = ids[(size_t)e * cap + j];
-        int sc = c_topo.f2c[id / NC], dc = c_topo.f2c[id % NC];
+        int sc = g_topo.f2c[id / NC], dc = g_topo.f2c[id % NC];
         if (sc < 0 || dc < 0) continue;
-        int can = c_topo.rot[seat][sc] * NB + c_topo.rot[seat][dc];
+        int can = g_topo.rot[seat][sc] * NB + g_topo.rot[seat][dc];
         uint64_t h = hash3(seed ^ 0xA5A5A5A5ull, ply, ((uint64_t)e << 16) ^ (uint64_t)can);
         float r1 = u01(h), r2 = u01(mix64(h)), r3 = u01(mix64(h ^ 0x5bd1e995ull));
         float logit = sqrtf(-2.f * logf(r1)) * cosf(6.2831853f * r2);
@@ -215,11 +244,14 @@ __global__ void sample_softmax_kernel(int n, const int8_t *turn, const int32_t *
 // ---------------------------------------------------------------------------
 // Host-side state
 // ---------------------------------------------------------------------------
+constexpr int OBS_TICKETS = 256;  // observation launches that may be in flight on one GPU at once
 struct DeviceState {
     bool topo = false, zob = false, obs = false;
     const int8_t *pool = nullptr;
     int pool_size = 0;
     int sms = 0, rule_blocks_per_sm = 0, obs_blocks_per_sm = 0;
+    int *obs_ticket = nullptr;             // OBS_TICKETS x {next unit, finished CTAs}, zero between launches
+    std::atomic<unsigned> obs_calls{0};
 };
 constexpr int MAX_DEV = 64;
 static DeviceState g_dev[MAX_DEV];
@@ -261,6 +293,20 @@ static int check_batch(const jq_batch *b) {
                           b->hist_count, b->bel_code, b->remaining, b->rem_tracked};
     for (const void *p : ptrs)
         if (!p) return fail(JQ_ERR_ARG, "a batch field pointer is null");
+    const void *wide[] = {b->move_count, b->active_eat, b->passive_surv, b->death_step, b->death_loc, b->cell_pid,
+                          b->zobrist, b->move_counter, b->mslc, b->cm_direct_lo, b->cm_direct_hi,
+                          b->cm_direct_type, b->cm_last_direct_step, b->cm_direct_other, b->cm_chain_lo,
+                          b->cm_chain_hi, b->cm_chain_type, b->cm_last_chain_step, b->cm_eaten_lo, b->cm_eaten_hi,
+                          b->cm_rank_floor_step, b->hist_src, b->hist_dst, b->hist_count, b->remaining};
+    for (const void *p : wide)
+        if ((uintptr_t)p & 1) return fail(JQ_ERR_ARG, "a multi-byte batch field is misaligned");
+    if (((uintptr_t)b->zobrist | (uintptr_t)b->cm_direct_lo | (uintptr_t)b->cm_direct_hi | (uintptr_t)b->cm_chain_lo |
+         (uintptr_t)b->cm_chain_hi | (uintptr_t)b->cm_eaten_lo | (uintptr_t)b->cm_eaten_hi) & 7)
+        return fail(JQ_ERR_ARG, "64-bit batch fields must be 8-byte aligned");
+    if (((uintptr_t)b->move_counter | (uintptr_t)b->mslc | (uintptr_t)b->hist_count) & 3)
+        return fail(JQ_ERR_ARG, "32-bit batch fields must be 4-byte aligned");
+    if ((uintptr_t)b->bel_code & 15) return fail(JQ_ERR_ARG, "bel_code must be 16-byte aligned");
+    if (b->rules != JQ_RULES_BATCHED && b->rules != JQ_RULES_GAMESTATE) return fail(JQ_ERR_ARG, "unknown rules value");
     return JQ_OK;
 }
 
@@ -324,11 +370,15 @@ int jq_init(int device) {
     static bool built = false;
     if (!built) { build_topo(host_topo); built = true; }
     CU(cudaMemcpyToSymbol(c_topo, &host_topo, sizeof(Topo)));
+    CU(cudaMemcpyToSymbol(g_topo, &host_topo, sizeof(Topo)));
     CU(cudaFuncSetAttribute(rules_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rule_smem()));
     CU(cudaFuncSetAttribute(obs_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)obs_smem()));
     CU(cudaDeviceGetAttribute(&st.sms, cudaDevAttrMultiProcessorCount, device));
     CU(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&st.rule_blocks_per_sm, rules_kernel, RULE_THREADS, rule_smem()));
     CU(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&st.obs_blocks_per_sm, obs_kernel, OBS_THREADS, obs_smem()));
+    if (st.obs_blocks_per_sm > OBS_MIN_CTAS) st.obs_blocks_per_sm = OBS_MIN_CTAS;
+    CU(cudaMalloc(&st.obs_ticket, sizeof(int) * 2 * OBS_TICKETS));
+    CU(cudaMemset(st.obs_ticket, 0, sizeof(int) * 2 * OBS_TICKETS));
     st.topo = true;
     return JQ_OK;
 }
@@ -416,6 +466,19 @@ int jq_init_beliefs(const jq_batch *b, int32_t show_mode, void *stream) {
     if (rc) return rc;
     a.flags = DO_BELIEF_INIT;
     return launch_rules(a, (cudaStream_t)stream);
+}
+
+int jq_rehash(const jq_batch *b, int32_t show_mode, void *stream) {
+    int rc = check_batch(b);
+    if (rc) return rc;
+    if (show_mode < 0 || show_mode > 2) return fail(JQ_ERR_ARG, "show_mode must be 0, 1 or 2");
+    DeviceState *st;
+    rc = current_dev(st);
+    if (rc) return rc;
+    if (!st->zob) return fail(JQ_ERR_NOT_READY, "Zobrist tables not uploaded");
+    rehash_kernel<<<(b->n + 7) / 8, 256, 0, (cudaStream_t)stream>>>(*b, show_mode);
+    CU(cudaGetLastError());
+    return JQ_OK;
 }
 
 int jq_step(const jq_batch *b, const int32_t *d_world_actions, int32_t show_mode, const jq_step_out *out,
@@ -545,6 +608,8 @@ int jq_observe(const jq_batch *b, const int8_t *d_observers, int32_t seats_per_e
     if (seats_per_env < 1 || seats_per_env > 4) return fail(JQ_ERR_ARG, "seats_per_env must be 1..4");
     if (show_mode < 0 || show_mode > 2) return fail(JQ_ERR_ARG, "show_mode must be 0, 1 or 2");
     if (!d_spatial || !d_global) return fail(JQ_ERR_ARG, "observation outputs missing");
+    if (((uintptr_t)d_spatial & 3) || ((uintptr_t)d_global & 3))
+        return fail(JQ_ERR_ARG, "observation outputs must be 4-byte aligned float arrays");
     if (!d_observers && seats_per_env != 1 && seats_per_env != 4)
         return fail(JQ_ERR_ARG, "observers required unless seats_per_env is 1 or 4");
     DeviceState *st;
@@ -552,10 +617,12 @@ int jq_observe(const jq_batch *b, const int8_t *d_observers, int32_t seats_per_e
     if (rc) return rc;
     if (!st->topo || !st->obs) return fail(JQ_ERR_NOT_READY, "jq_init / jq_upload_obs_tables missing");
     size_t units = (size_t)b->n * seats_per_env;
+    if (units > (size_t)INT32_MAX / 2) return fail(JQ_ERR_ARG, "too many observation units for one call");
     size_t grid = (size_t)st->sms * (st->obs_blocks_per_sm > 0 ? st->obs_blocks_per_sm : 1);
     if (grid > units) grid = units;
-    obs_kernel<<<(unsigned)grid, OBS_THREADS, obs_smem(), (cudaStream_t)stream>>>(*b, d_observers, seats_per_env,
-                                                                                   show_mode, d_spatial, d_global);
+    int *ticket = st->obs_ticket + 2 * (st->obs_calls.fetch_add(1) % OBS_TICKETS);
+    obs_kernel<<<(unsigned)grid, OBS_THREADS, obs_smem(), (cudaStream_t)stream>>>(
+        *b, d_observers, seats_per_env, show_mode, d_spatial, d_global, ticket);
     CU(cudaGetLastError());
     return JQ_OK;
 }

@@ -1,45 +1,97 @@
 // jq_obs.cuh -- 317-channel observation encoder (observation.py:598-1651).
 //
-// One CTA per (env, observer) unit at a time, persistent grid.  A unit is
-// 317 planes x 289 cells of float32 (366,452 B) plus 28 globals, almost all
-// zeros.  Layout of the work:
+// A unit is one (env, observer) pair: 317 planes x 289 cells of float32
+// (366,452 B) plus 28 globals, almost all zeros or ones.
 //
-//  * staging, once per unit: thread p < 120 turns piece p's state into the
-//    set of channels it lights with 1.0 -- a 320-bit mask (ten 32-bit words,
-//    one per 32-channel chunk) at one canonical cell -- plus the few
-//    channels that carry other values (belief vectors, kill counts,
-//    recency) and, for a dead piece, its death-reason cell;
-//  * ten 32-channel chunks, double-buffered in shared memory: scatter a
-//    chunk (one mask word per piece, plane fills for the constant groups),
-//    then one thread streams the chunk's 16-byte-aligned body to HBM with a
-//    TMA bulk store (cp.async.bulk ... bulk_group, L2 evict-first) while the
-//    CTA scatters the next chunk into the other buffer.  The 0-3 floats
-//    either side of the aligned body go out as plain stores.  A buffer is
-//    cleared after its bulk store has read it (cp.async.bulk.wait_group.read).
+// A unit is first described in shared memory as a bitstream with one bit per
+// output float in output order (the float is 1.0, else 0.0) plus a list of
+// exceptions -- (float index, value) for every float holding another value
+// (belief probability, kill count / 3, recency, progress, -1 of a history
+// source), about a thousand per unit.  The stream starts 4 - head bits in,
+// where head (0..3) is the number of floats before the unit's first 16-byte
+// boundary in global memory (a unit is 91,613 floats, so its base is only
+// 4-byte aligned); every aligned float4 of the output then owns one 4-bit
+// nibble of a 32-bit word.
 //
-// Every output byte is written once; values go straight to their canonical
-// cell (the observer's rotation applied per cell), which equals the
-// reference's world-frame build followed by rotate_planes.
+// Persistent CTAs of 12 warps, specialised:
+//  * 4 staging warps take units in memory order through an atomic ticket
+//    and build unit k+1 in one of two shared buffers (thread p sets the bits
+//    piece p lights at its canonical cell with shared atomicOr and appends
+//    its exceptions; then history, constant and board-static planes; the
+//    globals go straight to HBM);
+//  * 8 streaming warps write unit k from the other buffer: warp w one
+//    contiguous slab of the unit's aligned float4s, each float4 one shared
+//    word, a shift, four selects and a 16-byte store -- no branch -- and,
+//    after a barrier among them, the exception list as 4-byte stores over
+//    the lines just written (still in L2).
+// Named barriers hand the buffers back and forth (full / empty per buffer),
+// so staging latency -- dependent global loads per piece -- hides behind
+// the previous unit's stream.  Taking units in memory order keeps the units
+// being written at any moment in one compact window of the output: CTAs
+// that drift apart under a static unit-per-CTA stride spread the dirty
+// lines over the whole buffer and lose about a quarter of the DRAM write
+// bandwidth (write microbenchmark on this GPU).
+//
+// Values go straight to their canonical cell (the observer's rotation
+// applied per cell), which equals the reference's world-frame build
+// followed by rotate_planes.  Every output byte is written once.
 #pragma once
 #include "jq_rules.cuh"
 
 namespace jq {
 
-constexpr int OBS_THREADS = 256;
-constexpr int CHUNK = 32;                                // channels per buffer (= one mask word)
-constexpr int NCHUNK = (OBS_CH + CHUNK - 1) / CHUNK;     // 10
-constexpr int BUF_FLOATS = CHUNK * NC + 4;               // +3 floats of alignment slack, 16-byte multiple
-static_assert(BUF_FLOATS % 4 == 0, "buffers must keep 16-byte alignment");
+constexpr int OBS_STREAM_WARPS = 8;
+constexpr int OBS_STAGE_WARPS = 4;
+constexpr int OBS_STAGE_THREADS = 32 * OBS_STAGE_WARPS;                      // 128 >= 120 pieces
+constexpr int OBS_THREADS = 32 * (OBS_STREAM_WARPS + OBS_STAGE_WARPS);      // 384
+constexpr int OBS_WORDS = (OBS_FLOATS + 8 + 31) / 32;  // 2,864 words per stream
+constexpr int OBS_WORDS4 = (OBS_WORDS + 3) / 4;         // in uint4
+constexpr int STAT_MAX = NB * 5;                        // (static plane, cell) pairs, upper bound
+// named barriers (0 is __syncthreads)
+constexpr int BAR_FULL0 = 1, BAR_EMPTY0 = 3, BAR_STAGE = 5, BAR_STREAM = 6;
 
-struct __align__(16) ObsSmem {
-    float buf[2][BUF_FLOATS];
-    uint64_t type_lo[12], type_hi[12];  // observer-own pids of each tracked type
-    int16_t rotf[NC];                   // world flat -> canonical flat for this observer
-    int16_t hist_s[HIST], hist_d[HIST];
-    int32_t dead_const[3], flag_const[4];
+#ifndef OBS_MIN_CTAS
+#define OBS_MIN_CTAS 2
+#endif
+
+// plane kinds (which value an exception float of the plane takes)
+enum : uint8_t { K_BIN = 0, K_CONST = 1, K_HIST = 2, K_BEL = 3, K_KILL = 4, K_REC = 5 };
+
+__host__ __device__ constexpr uint8_t plane_kind(int ch) {
+    return (ch >= 12 && ch < 24) || (ch >= 27 && ch < 51) ? K_BEL
+           : (ch >= 51 && ch < 58) || ch == 64 || ch == 65 ? K_CONST
+           : (ch >= 129 && ch < 161)                        ? K_HIST
+           : (ch >= 211 && ch < 223)                        ? K_KILL
+           : (ch >= 253 && ch < 257)                        ? K_REC
+                                                            : K_BIN;
+}
+
+// Exceptions per unit, upper bound: beliefs 90 x 12, kill counts 60 x 12,
+// recency 60 x 4, progress 2 x 289, history 32.
+constexpr int EXC_MAX = 90 * 12 + 60 * 12 + 60 * 4 + 2 * NC + HIST;  // 2,650
+
+// One staged unit.
+struct __align__(16) UnitBuf {
+    uint32_t bits[OBS_WORDS4 * 4];
+    int32_t exc_pos[EXC_MAX];  // output float index of each exception
+    float exc_val[EXC_MAX];
+    float cval[2];             // progress planes 64, 65
+    int exc_n;
+    int u;                     // unit index, -1: no more units
 };
 
-__device__ __forceinline__ void setb(uint32_t *m, int ch) { m[ch >> 5] |= 1u << (ch & 31); }
+struct __align__(16) ObsSmem {
+    UnitBuf buf[2];
+    uint64_t type_lo[12], type_hi[12];  // observer-own pids of each tracked type (staging only)
+    int16_t rotf[NC];                   // world flat -> canonical flat for the staged observer
+    uint16_t stat[STAT_MAX];            // board-static bits: (plane - 58) * 289 + world flat
+    int stat_n;
+    int ticket, next_o;   // next unit for the staging warps and its observer
+    uint8_t kind[OBS_CH + 3];
+};
+
+__device__ __forceinline__ void bar_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+__device__ __forceinline__ void bar_arrive(int id, int n) { asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory"); }
 
 __device__ __forceinline__ bool in_back_two(int seat, int zx, int zy) {
     switch (seat) {  // observation.py:1378-1387
@@ -58,302 +110,373 @@ __device__ __forceinline__ float bel_value(int code, int t) {
     return 0.f;
 }
 
-__device__ __forceinline__ uint32_t smem_addr(const void *p) {
-    return (uint32_t)__cvta_generic_to_shared(p);
-}
+__device__ __forceinline__ void set_bit(uint32_t *s, int q) { atomicOr(&s[q >> 5], 1u << (q & 31)); }
 
-__device__ __forceinline__ void bulk_store(float *gdst, const float *ssrc, uint32_t bytes, uint64_t policy) {
-    asm volatile("cp.async.bulk.global.shared::cta.bulk_group.L2::cache_hint [%0], [%1], %2, %3;"
-                 :: "l"(gdst), "r"(smem_addr(ssrc)), "r"(bytes), "l"(policy) : "memory");
-    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-}
-__device__ __forceinline__ void bulk_wait_read_le1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
-__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-
-// Per-piece write set of one unit (thread p < 120 holds piece p's).
-struct PieceWrites {
-    uint32_t ones[NCHUNK];  // channels lit with 1.0 at cellA
-    int cellA;              // canonical cell, -1 none
-    int cellB, chB;         // death-reason write of a dead piece
-    int bel_base;           // 12 / 27 / 39 for teammate / left / right beliefs, -1 none
-    int code;               // belief code of the piece for this observer
-    uint32_t kill3;         // per tracked type: min(count, 3) in 2 bits (channels 211..222)
-    float rec[4];           // recency values (channels 253..256), 0 = none
+// Writes one unit's bitstream and exception list; stream position of float
+// (ch, cell) is its output index ch * 289 + cell shifted by qoff = 4 - head.
+struct Stager {
+    UnitBuf &B;
+    int qoff;
+    __device__ __forceinline__ int q(int ch, int cell) const { return ch * NC + cell + qoff; }
+    __device__ __forceinline__ void one(int ch, int cell) { set_bit(B.bits, q(ch, cell)); }
+    __device__ __forceinline__ void exception(int j, float v) {
+        const int i = atomicAdd(&B.exc_n, 1);
+        if (i < EXC_MAX) {
+            B.exc_pos[i] = j;
+            B.exc_val[i] = v;
+        }
+    }
+    // a float with value v (0 leaves it at 0, 1 is a plain bit, anything else an exception)
+    __device__ __forceinline__ void value(int ch, int cell, float v) {
+        if (v == 0.f) return;
+        if (v == 1.f) one(ch, cell);
+        else exception(ch * NC + cell, v);
+    }
+    __device__ __forceinline__ void ones(int ch0, uint32_t m, int cell) {
+        while (m) {
+            const int i = __ffs(m) - 1;
+            m &= m - 1;
+            one(ch0 + i, cell);
+        }
+    }
+    // all 289 floats of plane ch in stream s; thread k of nthreads covers some words
+    __device__ __forceinline__ void fill_plane(uint32_t *s, int ch, int k, int nthreads) {
+        const int q0 = q(ch, 0), q1 = q0 + NC, w0 = q0 >> 5, w1 = (q1 - 1) >> 5;
+        for (int w = w0 + k; w <= w1; w += nthreads) {
+            const int lo = q0 > w * 32 ? q0 - w * 32 : 0, hi = q1 < w * 32 + 32 ? q1 - w * 32 : 32;
+            const uint32_t m = (hi - lo == 32 ? ~0u : ((1u << (hi - lo)) - 1u)) << lo;
+            atomicOr(&s[w], m);
+        }
+    }
 };
 
-__device__ void stage_piece(const jq_batch &b, int e, int o, int mode, const ObsSmem &S, int p, PieceWrites &pw) {
+// Bits [pos, pos + 30) of a 120-bit pid set held as (lo, hi).
+__device__ __forceinline__ uint32_t pid_field30(uint64_t lo, uint64_t hi, int pos) {
+    if (pos + 30 <= 64) return (uint32_t)(lo >> pos) & 0x3FFFFFFFu;
+    if (pos >= 64) return (uint32_t)(hi >> (pos - 64)) & 0x3FFFFFFFu;
+    return (uint32_t)((lo >> pos) | (hi << (64 - pos))) & 0x3FFFFFFFu;
+}
+
+// The first min(max(count, 0), n) planes of a threshold group (plane g lit
+// when count >= g + 1).
+__device__ __forceinline__ uint32_t thresh_mask(int count, int n) {
+    const int c = count < 0 ? 0 : (count > n ? n : count);
+    return (1u << c) - 1u;
+}
+
+// Piece p's contribution for observer o (observation.py:1233-1569 per piece).
+// Every field the piece may need is loaded up front, so the staging warps
+// wait for memory once rather than once per branch.
+__device__ void stage_piece(const jq_batch &b, int e, int o, int mode, const ObsSmem &S, Stager &st, int p) {
     const int tm = (o + 2) & 3, left = (o + 1) & 3, right = (o + 3) & 3, oteam = o & 1;
-#pragma unroll
-    for (int i = 0; i < NCHUNK; ++i) pw.ones[i] = 0;
-    pw.cellA = pw.cellB = pw.chB = pw.bel_base = -1;
-    pw.code = 0;
-    pw.kill3 = 0;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) pw.rec[i] = 0.f;
     const size_t q = PI(e, p), k = OI(e, o, p);
     const int alive_raw = b.alive[q];
     const int s = b.piece_seat[q];
-    const int team = s >= 0 ? (s & 1) : 1;  // numpy _SEAT_TEAM[-1] is EAST's team
     const int x = b.pos_x[q], y = b.pos_y[q], zx = b.zero_x[q], zy = b.zero_y[q];
-    const int mcnt = b.move_count[q];
+    const int ptype = b.piece_type[q];
+    const int mcnt = b.move_count[q], ae_raw = b.active_eat[q], ps_raw = b.passive_surv[q];
+    const int dstep = b.death_step[q], dreason = b.death_reason[q], dloc = b.death_loc[q];
+    const int code = b.bel_code[k];
+    const uint64_t dlo = b.cm_direct_lo[k], dhi = b.cm_direct_hi[k];
+    const uint64_t clo = b.cm_chain_lo[k], chi = b.cm_chain_hi[k];
+    const uint64_t elo = b.cm_eaten_lo[k], ehi = b.cm_eaten_hi[k];
+    const int dtype = b.cm_direct_type[k], ctype = b.cm_chain_type[k];
+    const int other = b.cm_direct_other[k], fl = b.cm_rank_floor[k];
+    const int is_g = b.cm_is_gongb[k], not_g = b.cm_not_gongb[k], atk_g = b.cm_atk_gongb[k];
+    const int last_d = b.cm_last_direct_step[k], last_c = b.cm_last_chain_step[k], last_f = b.cm_rank_floor_step[k];
+    const int cur = b.move_counter[e];
+    const size_t kl = OI(e, left, p), kr = OI(e, right, p);
+    const int lc = __popcll(b.cm_direct_lo[kl]) + __popcll(b.cm_direct_hi[kl]) + b.cm_direct_other[kl];
+    const int rc = __popcll(b.cm_direct_lo[kr]) + __popcll(b.cm_direct_hi[kr]) + b.cm_direct_other[kr];
+    const int lg = b.cm_is_gongb[kl] && b.cm_is_gongb[kr];
+    const bool patk = b.cm_atk_gongb[kl] || b.cm_atk_gongb[kr];
+
+    const int team = s >= 0 ? (s & 1) : 1;  // numpy _SEAT_TEAM[-1] is EAST's team
     const bool own_pid = (p / 30) == o;
+    int cell;
     if (alive_raw) {
         if (!(x >= 0 && x < 17 && y >= 0 && y < 17)) return;
-        pw.cellA = S.rotf[y * 17 + x];
-        const int ti = tracked_idx(b.piece_type[q]);
-        pw.code = b.bel_code[k];
-        if (s == o && ti >= 0) setb(pw.ones, ti);
+        cell = S.rotf[y * 17 + x];
+        const int ti = tracked_idx(ptype);
+        if (s == o && ti >= 0) st.one(ti, cell);
+        int base = -1;
         if (s == tm) {
-            pw.bel_base = 12;
-            if (mode == SM_DARK) setb(pw.ones, 24);
+            base = 12;
+            if (mode == SM_DARK) st.one(24, cell);
         }
-        if (s == left) { setb(pw.ones, 25); pw.bel_base = 27; }
-        if (s == right) { setb(pw.ones, 26); pw.bel_base = 39; }
+        if (s == left) { st.one(25, cell); base = 27; }
+        if (s == right) { st.one(26, cell); base = 39; }
+        if (base >= 0)
+            for (int t = 0; t < 12; ++t) st.value(base + t, cell, bel_value(code, t));
         const int half = team == oteam ? 0 : 4;
-        setb(pw.ones, 66 + half + (mcnt < 3 ? mcnt : 3));
-        const int ae = b.active_eat[q] < 3 ? b.active_eat[q] : 3, ps = b.passive_surv[q] < 3 ? b.passive_surv[q] : 3;
-        for (int g = 0; g <= ae; ++g) setb(pw.ones, 74 + half + g);
-        for (int g = 0; g <= ps; ++g) setb(pw.ones, 82 + half + g);
-        const int sch = c_topo.slot_ch[p % 30];
-        setb(pw.ones, 104 + (sch < 0 ? 24 : sch));
+        st.one(66 + half + (mcnt < 3 ? mcnt : 3), cell);
+        const int ae = ae_raw < 3 ? ae_raw : 3, ps = ps_raw < 3 ? ps_raw : 3;
+        st.ones(74 + half, thresh_mask(ae + 1, 4), cell);
+        st.ones(82 + half, thresh_mask(ps + 1, 4), cell);
+        const int sch = g_topo.slot_ch[p % 30];
+        st.one(104 + (sch < 0 ? 24 : sch), cell);
         if (team != oteam) {
             // layer 1 + 3 (observation.py:1295-1392, 1474-1569)
-            const uint64_t dlo = b.cm_direct_lo[k], dhi = b.cm_direct_hi[k];
-            const uint64_t clo = b.cm_chain_lo[k], chi = b.cm_chain_hi[k];
-            const int dtype = b.cm_direct_type[k], ctype = b.cm_chain_type[k];
-            const int other = b.cm_direct_other[k], fl = b.cm_rank_floor[k];
             const int mine = __popcll(dlo) + __popcll(dhi), chn = __popcll(clo) + __popcll(chi);
-            for (int g = 0; g < 3; ++g) {
-                if (mine >= g + 1) setb(pw.ones, 173 + g);
-                if (other >= g + 1) setb(pw.ones, 176 + g);
-                if (chn >= g + 1) setb(pw.ones, 191 + g);
-            }
-            for (int t = 0; t < 12; ++t) {
-                if ((dtype >> t) & 1) setb(pw.ones, 161 + t);
-                if ((ctype >> t) & 1) setb(pw.ones, 179 + t);
-            }
-            for (int g = 0; g < 9; ++g)
-                if (fl >= g + 1) setb(pw.ones, 194 + g);
-            if (b.cm_is_gongb[k]) setb(pw.ones, 203);
-            if (b.cm_not_gongb[k]) setb(pw.ones, 204);
-            if (in_back_two(s, zx, zy) && mcnt == 0 && !b.cm_atk_gongb[k]) setb(pw.ones, 205);
-            for (int sl = 0; sl < 30; ++sl) {
-                const int gp = o * 30 + sl;
-                const bool on = gp < 64 ? ((dlo >> gp) & 1ull) : ((dhi >> (gp - 64)) & 1ull);
-                if (on) setb(pw.ones, 223 + sl);
-            }
+            st.ones(173, thresh_mask(mine, 3), cell);
+            st.ones(176, thresh_mask(other, 3), cell);
+            st.ones(191, thresh_mask(chn, 3), cell);
+            st.ones(161, (uint32_t)dtype & 0xFFFu, cell);
+            st.ones(179, (uint32_t)ctype & 0xFFFu, cell);
+            st.ones(194, thresh_mask(fl, 9), cell);
+            if (is_g) st.one(203, cell);
+            if (not_g) st.one(204, cell);
+            if (in_back_two(s, zx, zy) && mcnt == 0 && !atk_g) st.one(205, cell);
+            st.ones(223, pid_field30(dlo, dhi, o * 30), cell);
             for (int t = 0; t < 12; ++t) {
                 const int c = __popcll(dlo & S.type_lo[t]) + __popcll(dhi & S.type_hi[t]);
-                pw.kill3 |= (uint32_t)(c < 3 ? c : 3) << (2 * t);
+                if (c) st.value(211 + t, cell, __fdiv_rn((float)(c < 3 ? c : 3), 3.0f));
             }
-            const int cur = b.move_counter[e];
-            const int lasts[4] = {b.cm_last_direct_step[k], b.cm_last_direct_step[k], b.cm_last_chain_step[k],
-                                  b.cm_rank_floor_step[k]};
+            const int lasts[4] = {last_d, last_d, last_c, last_f};
 #pragma unroll
             for (int pl = 0; pl < 4; ++pl) {
-                if (lasts[pl] < 0) continue;
-                int el = cur - lasts[pl];
-                el = el < 0 ? 0 : (el > RECENCY_LEN - 1 ? RECENCY_LEN - 1 : el);
-                pw.rec[pl] = g_recency[pl * RECENCY_LEN + el];
+                float r = 0.f;
+                if (lasts[pl] >= 0) {
+                    int el = cur - lasts[pl];
+                    el = el < 0 ? 0 : (el > RECENCY_LEN - 1 ? RECENCY_LEN - 1 : el);
+                    r = g_recency[pl * RECENCY_LEN + el];
+                }
+                if (r > 0.f) st.value(253 + pl, cell, r);
             }
         }
         if (s == o) {  // layer 2 (observation.py:1394-1459)
-            const size_t kl = OI(e, left, p), kr = OI(e, right, p);
-            const int lc = __popcll(b.cm_direct_lo[kl]) + __popcll(b.cm_direct_hi[kl]) + b.cm_direct_other[kl];
-            const int rc = __popcll(b.cm_direct_lo[kr]) + __popcll(b.cm_direct_hi[kr]) + b.cm_direct_other[kr];
-            const int pub = lc < rc ? lc : rc;
-            for (int g = 0; g < 3; ++g)
-                if (pub >= g + 1) setb(pw.ones, 206 + g);
-            if (b.cm_is_gongb[kl] && b.cm_is_gongb[kr]) setb(pw.ones, 209);
-            const bool patk = b.cm_atk_gongb[kl] || b.cm_atk_gongb[kr];
-            if (in_back_two(s, zx, zy) && mcnt == 0 && !patk) setb(pw.ones, 210);
+            st.ones(206, thresh_mask(lc < rc ? lc : rc, 3), cell);
+            if (lg) st.one(209, cell);
+            if (in_back_two(s, zx, zy) && mcnt == 0 && !patk) st.one(210, cell);
         }
     } else {
-        if (b.death_step[q] != -1) {  // GameState.deaths keys
-            const int r = b.death_reason[q];
-            const int ridx = (r >= 0 && r <= 2) ? r : (r == -1 ? 2 : -1);
+        if (dstep != -1) {  // GameState.deaths keys
+            const int ridx = (dreason >= 0 && dreason <= 2) ? dreason : (dreason == -1 ? 2 : -1);
             const int grp = s == o ? 0 : s == tm ? 3 : s == left ? 6 : s == right ? 9 : -1;
-            if (ridx >= 0 && b.death_step[q] > 0 && grp >= 0) {
+            if (ridx >= 0 && dstep > 0 && grp >= 0) {
                 // numpy index semantics of death_loc // 17, death_loc % 17 (-1 -> row 16, col 16)
-                const int f = b.death_loc[q];
-                int yy = f >= 0 ? f / 17 : -((-f + 16) / 17);
-                const int xx = ((f % 17) + 17) % 17;
+                int yy = dloc >= 0 ? dloc / 17 : -((-dloc + 16) / 17);
+                const int xx = ((dloc % 17) + 17) % 17;
                 if (yy < 0) yy += 17;
-                if (yy >= 0 && yy < 17) { pw.chB = 90 + grp + ridx; pw.cellB = S.rotf[yy * 17 + xx]; }
+                if (yy >= 0 && yy < 17) st.one(90 + grp + ridx, S.rotf[yy * 17 + xx]);
             }
         }
         if (!(zx >= 0 && zx < 17 && zy >= 0 && zy < 17)) return;
-        pw.cellA = S.rotf[zy * 17 + zx];
-        if (b.death_step[q] != -1) setb(pw.ones, 102 + (team == oteam ? 0 : 1));
+        cell = S.rotf[zy * 17 + zx];
+        if (dstep != -1) st.one(102 + (team == oteam ? 0 : 1), cell);
     }
     if (own_pid) {  // layer 4: observer-own pid at its cell (alive) or zero cell (dead)
-        const uint64_t elo = b.cm_eaten_lo[k], ehi = b.cm_eaten_hi[k];
-        const int opps[2] = {left, right};
-        for (int h = 0; h < 2; ++h)
-            for (int sl = 0; sl < 30; ++sl) {
-                const int gp = opps[h] * 30 + sl;
-                const bool on = gp < 64 ? ((elo >> gp) & 1ull) : ((ehi >> (gp - 64)) & 1ull);
-                if (on) setb(pw.ones, 257 + h * 30 + sl);
-            }
+        st.ones(257, pid_field30(elo, ehi, left * 30), cell);
+        st.ones(287, pid_field30(elo, ehi, right * 30), cell);
     }
 }
 
-// Grid: persistent; CTA-stride over output units u = e * seats + k.
-__global__ void __launch_bounds__(OBS_THREADS, 3) obs_kernel(jq_batch b, const int8_t *__restrict__ observers,
-                                                             int seats, int mode, float *spatial, float *global) {
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    ObsSmem &S = *reinterpret_cast<ObsSmem *>(smem_raw);
-    const int tid = threadIdx.x;
-    uint64_t policy = 0;
-    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
-    for (int k = tid; k < 2 * BUF_FLOATS; k += OBS_THREADS) (&S.buf[0][0])[k] = 0.f;
-    int qn = 0;  // chunks issued by this CTA so far (selects the buffer)
-    const size_t units = (size_t)b.n * seats;
-    for (size_t u = blockIdx.x; u < units; u += gridDim.x) {
-        const int e = (int)(u / seats);
-        int o = observers ? observers[u] : (seats == 1 ? b.turn[e] : (int)(u % seats));
-        o &= 3;
-        const int tm = (o + 2) & 3, left = (o + 1) & 3, right = (o + 3) & 3;
-        // ---------------- staging ----------------
-        __syncthreads();  // previous unit's readers of the staged tables are done
-        for (int f = tid; f < NC; f += OBS_THREADS) S.rotf[f] = c_topo.rotf[o][f];
-        if (tid < HIST) {
-            const int hc = b.hist_count[e], n = hc < HIST ? hc : HIST;
-            int s = -1, d = -1;
-            if (tid < n) {
-                const int slot = (hc - 1 - tid) & (HIST - 1);
-                s = b.hist_src[(size_t)e * HIST + slot];
-                d = b.hist_dst[(size_t)e * HIST + slot];
-                if (s < 0 || s >= NC || d < 0 || d >= NC) s = d = -1;
-            }
-            S.hist_s[tid] = (int16_t)s;
-            S.hist_d[tid] = (int16_t)d;
-        }
-        if (tid >= 32 && tid < 44) {
-            const int t = tid - 32;
-            uint64_t lo = 0, hi = 0;
-            for (int s = 0; s < 30; ++s)
-                if (tracked_idx(b.piece_type[PI(e, o * 30 + s)]) == t) set_pid_bit(lo, hi, o * 30 + s);
-            S.type_lo[t] = lo;
-            S.type_hi[t] = hi;
-        }
-        if (tid >= 64 && tid < 67) {
-            const int ord[3] = {tm, left, right};
-            S.dead_const[tid - 64] = b.seat_dead[(size_t)e * 4 + ord[tid - 64]];
-        }
-        if (tid >= 96 && tid < 100) {
-            const int ord[4] = {o, tm, left, right};
-            S.flag_const[tid - 96] = b.seat_flag[(size_t)e * 4 + ord[tid - 96]];
-        }
-        if (tid >= 128 && tid < 128 + OBS_GL) {  // globals (observation.py:1623-1651)
-            const int j = tid - 128;
-            float v;
-            if (j < 24) {
-                v = (float)b.remaining[(size_t)e * 192 + (o * 4 + (j < 12 ? left : right)) * 12 + (j % 12)];
-            } else {
-                const int ord[4] = {o, tm, left, right};
-                v = b.seat_flag[(size_t)e * 4 + ord[j - 24]] ? 1.f : 0.f;
-            }
-            global[u * OBS_GL + j] = v;
-        }
-        const float prog_d = (float)fmin((double)b.mslc[e] / 200.0, 1.0);
-        const float prog_m = (float)fmin((double)b.move_counter[e] / 4000.0, 1.0);
-        __syncthreads();
-        PieceWrites pw;
-        if (tid < NP) stage_piece(b, e, o, mode, S, tid, pw);
-        else pw.cellA = pw.cellB = -1;
+__device__ __forceinline__ float bit_value(const UnitBuf &B, int j, int qoff) {
+    const int qq = j + qoff;
+    return ((B.bits[qq >> 5] >> (qq & 31)) & 1u) ? 1.f : 0.f;
+}
 
-        float *out = spatial + u * (size_t)OBS_FLOATS;
-        for (int c = 0; c < NCHUNK; ++c, ++qn) {
-            float *B = S.buf[qn & 1];
-            const int c0 = c * CHUNK, c1 = c0 + CHUNK < OBS_CH ? c0 + CHUNK : OBS_CH;
-            float *g = out + (size_t)c0 * NC;
-            const int pad = (int)(((uintptr_t)g >> 2) & 3);
-            float *cv = B + pad;
-            // ---- buffer reuse: the bulk store issued two chunks ago from B must have read it ----
-            if (qn >= 2) {
-                if (tid == 0) bulk_wait_read_le1();
-                __syncthreads();
-                float4 *B4 = reinterpret_cast<float4 *>(B);
-                const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
-                for (int k2 = tid; k2 < BUF_FLOATS / 4; k2 += OBS_THREADS) B4[k2] = z4;
-                __syncthreads();
-            }
-            // ---- scatter ----
-            if (pw.cellA >= 0) {
-                uint32_t m = pw.ones[c];
-                while (m) {
-                    const int bit = __ffs(m) - 1;
-                    m &= m - 1;
-                    cv[bit * NC + pw.cellA] = 1.f;
-                }
-                if (pw.bel_base >= 0 && pw.bel_base < c1 && pw.bel_base + 12 > c0)
-                    for (int t = 0; t < 12; ++t) {
-                        const int ch = pw.bel_base + t;
-                        if (ch < c0 || ch >= c1) continue;
-                        const float v = bel_value(pw.code, t);
-                        if (v != 0.f) cv[(ch - c0) * NC + pw.cellA] = v;
-                    }
-                if (pw.kill3 && 211 < c1 && 223 > c0)
-                    for (int t = 0; t < 12; ++t) {
-                        const int ch = 211 + t, cnt = (pw.kill3 >> (2 * t)) & 3;
-                        if (cnt && ch >= c0 && ch < c1) cv[(ch - c0) * NC + pw.cellA] = __fdiv_rn((float)cnt, 3.0f);
-                    }
-                if (253 < c1 && 257 > c0)
+__device__ __forceinline__ int unit_head(const float *spatial, int u) {
+    const float *out = spatial + (size_t)u * OBS_FLOATS;
+    return (int)((4 - (((uintptr_t)out >> 2) & 3)) & 3);
+}
+
+// Staging warps: build unit u (observer o of env e) into B.  t = thread in 0..127.
+__device__ __forceinline__ int unit_observer(const jq_batch &b, const int8_t *observers, int seats, int u) {
+    const int e = u / seats;
+    return (observers ? observers[u] : (seats == 1 ? b.turn[e] : u % seats)) & 3;
+}
+
+__device__ void stage_unit(const jq_batch &b, int seats, int mode, float *global, ObsSmem &S, UnitBuf &B, int u,
+                           int o, int head, int t) {
+    const int e = u / seats;
+    const int tm = (o + 2) & 3, left = (o + 1) & 3, right = (o + 3) & 3;
+    Stager st{B, 4 - head};
+    // init
+    {
+        uint4 *b4 = reinterpret_cast<uint4 *>(B.bits);
+        const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+        for (int k2 = t; k2 < OBS_WORDS4; k2 += OBS_STAGE_THREADS) b4[k2] = z;
+    }
+    for (int f = t; f < NC; f += OBS_STAGE_THREADS) S.rotf[f] = g_topo.rotf[o][f];
+    if (t < 32) {  // observer-own pids per tracked type: one load per lane, one ballot per type
+        const int ti = t < 30 ? tracked_idx(b.piece_type[PI(e, o * 30 + t)]) : -1;
+        const int pos = o * 30;
 #pragma unroll
-                    for (int pl = 0; pl < 4; ++pl) {
-                        const int ch = 253 + pl;
-                        if (pw.rec[pl] > 0.f && ch >= c0 && ch < c1) cv[(ch - c0) * NC + pw.cellA] = pw.rec[pl];
-                    }
-            }
-            if (pw.cellB >= 0 && pw.chB >= c0 && pw.chB < c1) cv[(pw.chB - c0) * NC + pw.cellB] = 1.f;
-            if (tid >= 128 && tid < 128 + HIST) {  // move history (observation.py:1207-1231)
-                const int d = tid - 128, ch = 129 + d;
-                if (ch >= c0 && ch < c1 && S.hist_s[d] >= 0) {
-                    cv[(ch - c0) * NC + S.rotf[S.hist_s[d]]] = -1.f;
-                    cv[(ch - c0) * NC + S.rotf[S.hist_d[d]]] = 1.f;
-                }
-            }
-            // constant planes (observation.py:984-1021) and board statics (343-383)
-            const int k_lo = c0 > 51 ? c0 : 51, k_hi = c1 < 66 ? c1 : 66;
-            for (int k2 = tid; k2 < (k_hi - k_lo) * NC; k2 += OBS_THREADS) {
-                const int ch = k_lo + k2 / NC, cell = k2 % NC;
-                float v = 0.f;
-                if (ch < 54) v = S.dead_const[ch - 51] ? 1.f : 0.f;
-                else if (ch < 58) v = S.flag_const[ch - 54] ? 1.f : 0.f;
-                else if (ch == 64) v = prog_d;
-                else if (ch == 65) v = prog_m;
-                else continue;
-                if (v != 0.f) cv[(ch - c0) * NC + cell] = v;
-            }
-            if (58 < c1 && 63 > c0)
-                for (int f = tid; f < NC; f += OBS_THREADS) {
-                    const int cc = c_topo.f2c[f];
-                    if (cc < 0) continue;
-                    const uint8_t fl = c_topo.flags[cc];
-                    const int cell = S.rotf[f];
-                    const int bits[5] = {F_CAMP, F_SH, F_RAIL, F_NINE, F_ARC};
-#pragma unroll
-                    for (int i = 0; i < 5; ++i)
-                        if ((fl & bits[i]) && 58 + i >= c0 && 58 + i < c1) cv[(58 + i - c0) * NC + cell] = 1.f;
-                }
-            fence_async_smem();
-            __syncthreads();
-            // ---- stream the chunk: aligned body by TMA bulk store, 0-3 floats each side plainly ----
-            const int n = (c1 - c0) * NC;
-            const int head = (4 - pad) & 3;
-            const int body = ((n - head) >> 2) << 2;
-            if (tid == 0 && body > 0) bulk_store(g + head, cv + head, (uint32_t)body * 4u, policy);
-            if (tid >= 32 && tid < 32 + head) __stcs(g + (tid - 32), cv[tid - 32]);
-            if (tid >= 64 && tid < 64 + (n - head - body)) {
-                const int j = head + body + (tid - 64);
-                __stcs(g + j, cv[j]);
+        for (int tt = 0; tt < 12; ++tt) {
+            const uint64_t m = __ballot_sync(0xffffffffu, ti == tt) & 0x3FFFFFFFu;
+            if (t == tt) {
+                S.type_lo[tt] = pos < 64 ? m << pos : 0ull;
+                S.type_hi[tt] = pos >= 64 ? m << (pos - 64) : (pos + 30 > 64 ? m >> (64 - pos) : 0ull);
             }
         }
     }
-    if (tid == 0) bulk_wait_all();
+    if (t == 32) B.cval[0] = (float)fmin((double)b.mslc[e] / 200.0, 1.0);
+    if (t == 33) B.cval[1] = (float)fmin((double)b.move_counter[e] / 4000.0, 1.0);
+    if (t >= 64 && t < 64 + OBS_GL) {  // globals (observation.py:1623-1651)
+        const int j = t - 64;
+        float v;
+        if (j < 24) {
+            v = (float)b.remaining[(size_t)e * 192 + (o * 4 + (j < 12 ? left : right)) * 12 + (j % 12)];
+        } else {
+            const int sf = j == 24 ? o : j == 25 ? tm : j == 26 ? left : right;
+            v = b.seat_flag[(size_t)e * 4 + sf] ? 1.f : 0.f;
+        }
+        global[(size_t)u * OBS_GL + j] = v;
+    }
+    if (t == 0) {
+        B.u = u;
+        B.exc_n = 0;
+    }
+    bar_sync(BAR_STAGE, OBS_STAGE_THREADS);
+    // pieces, then history / constants / statics (all bit writes are atomic)
+    if (t < NP) stage_piece(b, e, o, mode, S, st, t);
+    if (t < HIST) {  // move history (observation.py:1207-1231)
+        const int hc = b.hist_count[e], n = hc < HIST ? hc : HIST;
+        if (t < n) {
+            const int slot = (hc - 1 - t) & (HIST - 1);
+            const int s = b.hist_src[(size_t)e * HIST + slot], d = b.hist_dst[(size_t)e * HIST + slot];
+            if (s >= 0 && s < NC && d >= 0 && d < NC) {
+                const int cs = S.rotf[s], cd = S.rotf[d];
+                st.one(129 + t, cd);
+                if (cs != cd) st.exception((129 + t) * NC + cs, -1.f);  // the destination's +1 wins
+            }
+        }
+    } else {  // constant planes (observation.py:984-1021) and board statics (343-383)
+        const int k = t - HIST, nk = OBS_STAGE_THREADS - HIST;
+        uint32_t dead4 = 0, flag4 = 0;  // one load each: the env's four seat bytes
+        {
+            const uint8_t *sdp = b.seat_dead + (size_t)e * 4, *sfp = b.seat_flag + (size_t)e * 4;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                dead4 |= (sdp[i] ? 1u : 0u) << i;
+                flag4 |= (sfp[i] ? 1u : 0u) << i;
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < 7; ++j) {
+            const int sd = j == 0 ? tm : j == 1 ? left : j == 2 ? right : j == 3 ? o : j == 4 ? tm : j == 5 ? left : right;
+            const uint32_t on = ((j < 3 ? dead4 : flag4) >> sd) & 1u;
+            if (on) st.fill_plane(B.bits, 51 + j, k, nk);
+        }
+        for (int j = 0; j < 2; ++j) {
+            const float v = B.cval[j];
+            if (v == 1.f) st.fill_plane(B.bits, 64 + j, k, nk);
+            else if (v != 0.f)
+                for (int c = k; c < NC; c += nk) st.exception((64 + j) * NC + c, v);
+        }
+        for (int i = k; i < S.stat_n; i += nk) {
+            const int en = S.stat[i], pl = en / NC, f = en - pl * NC;
+            st.one(58 + pl, S.rotf[f]);
+        }
+    }
+}
+
+// Streaming warps: write unit B.u.  w = streaming warp 0..7, t = its thread 0..255.
+__device__ void stream_unit(const UnitBuf &B, float *spatial, int w, int lane) {
+    const int u = B.u, t = w * 32 + lane;
+    float *out = spatial + (size_t)u * OBS_FLOATS;
+    const int head = unit_head(spatial, u), qoff = 4 - head;
+    const int body4 = (OBS_FLOATS - head) >> 2;
+    // pass 1: every float as 0 / 1 -- the head and tail floats one by one, the
+    // aligned body as float4 (warp w: one contiguous slab), branch-free
+    if (t < head) out[t] = bit_value(B, t, qoff);
+    if (t >= 32 && t < 36) {
+        const int j = head + body4 * 4 + (t - 32);
+        if (j < OBS_FLOATS) out[j] = bit_value(B, j, qoff);
+    }
+    float4 *out4 = reinterpret_cast<float4 *>(out + head);
+    const int per = (body4 + OBS_STREAM_WARPS - 1) / OBS_STREAM_WARPS;
+    const int g0 = w * per, g1 = g0 + per < body4 ? g0 + per : body4;
+#pragma unroll 4
+    for (int g = g0 + lane; g < g1; g += 32) {
+        // float4 g holds output floats head + 4g .. +3 = stream bits 4g + 4 .. 4g + 7
+        const uint32_t nib = (B.bits[(g + 1) >> 3] >> (((g + 1) & 7) << 2)) & 15u;
+        out4[g] = make_float4((nib & 1u) ? 1.f : 0.f, (nib & 2u) ? 1.f : 0.f, (nib & 4u) ? 1.f : 0.f,
+                              (nib & 8u) ? 1.f : 0.f);
+    }
+    // pass 2: the exceptions, ordered after pass 1 by the streaming warps' barrier
+    bar_sync(BAR_STREAM, 32 * OBS_STREAM_WARPS);
+    const int n = B.exc_n < EXC_MAX ? B.exc_n : EXC_MAX;
+    for (int i = t; i < n; i += 32 * OBS_STREAM_WARPS) out[B.exc_pos[i]] = B.exc_val[i];
+}
+
+// Grid: persistent.  ticket[0] hands out units u = e * seats + k in order;
+// ticket[1] counts finished CTAs, and the last one resets both to zero for
+// the next launch that uses this ticket.
+__global__ void __launch_bounds__(OBS_THREADS, OBS_MIN_CTAS) obs_kernel(jq_batch b, const int8_t *__restrict__ observers,
+                                                                        int seats, int mode, float *spatial,
+                                                                        float *global, int *ticket) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    ObsSmem &S = *reinterpret_cast<ObsSmem *>(smem_raw);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    // once per CTA: plane kinds and the list of board-static bits (observation.py:343-383)
+    for (int ch = tid; ch < OBS_CH + 3; ch += OBS_THREADS) S.kind[ch] = ch < OBS_CH ? plane_kind(ch) : K_BIN;
+    if (tid == 0) S.stat_n = 0;
     __syncthreads();
+    for (int f = tid; f < NC; f += OBS_THREADS) {
+        const int cc = g_topo.f2c[f];
+        if (cc < 0) continue;
+        const uint8_t fl = g_topo.flags[cc];
+        const uint8_t fb[5] = {F_CAMP, F_SH, F_RAIL, F_NINE, F_ARC};
+#pragma unroll
+        for (int i = 0; i < 5; ++i)
+            if (fl & fb[i]) S.stat[atomicAdd(&S.stat_n, 1)] = (uint16_t)(i * NC + f);
+    }
+    __syncthreads();
+    const int units = b.n * seats;
+    if (warp < OBS_STREAM_WARPS) {
+        for (int k = 0;; ++k) {
+            const int bi = k & 1;
+            bar_sync(BAR_FULL0 + bi, OBS_THREADS);  // buffer bi staged
+            const UnitBuf &B = S.buf[bi];
+            if (B.u < 0) break;
+            stream_unit(B, spatial, warp, lane);
+            bar_arrive(BAR_EMPTY0 + bi, OBS_THREADS);  // buffer bi free again
+        }
+    } else {
+        const int t = tid - 32 * OBS_STREAM_WARPS;
+        // The next unit (and its observer) is fetched while the current one
+        // is staged, so the ticket and observer loads leave the critical path.
+        if (t == 0) {
+            const int u0 = atomicAdd(&ticket[0], 1);
+            S.ticket = u0;
+            S.next_o = u0 < units ? unit_observer(b, observers, seats, u0) : 0;
+        }
+        bar_sync(BAR_STAGE, OBS_STAGE_THREADS);
+        int u = S.ticket, o = S.next_o;
+        int k = 0;
+        for (;; ++k) {
+            const int bi = k & 1;
+            UnitBuf &B = S.buf[bi];
+            if (k >= 2) bar_sync(BAR_EMPTY0 + bi, OBS_THREADS);  // unit k - 2 streamed out of buffer bi
+            if (u >= units) {
+                if (t == 0) B.u = -1;
+                bar_arrive(BAR_FULL0 + bi, OBS_THREADS);
+                break;
+            }
+            int un = 0, on = 0;
+            if (t == 0) {
+                un = atomicAdd(&ticket[0], 1);
+                on = un < units ? unit_observer(b, observers, seats, un) : 0;
+            }
+            stage_unit(b, seats, mode, global, S, B, u, o, unit_head(spatial, u), t);
+            if (t == 0) { S.ticket = un; S.next_o = on; }
+            bar_sync(BAR_STAGE, OBS_STAGE_THREADS);  // unit staged; next ticket published
+            u = S.ticket;
+            o = S.next_o;
+            bar_arrive(BAR_FULL0 + bi, OBS_THREADS);
+            bar_sync(BAR_STAGE, OBS_STAGE_THREADS);  // everyone has read the next ticket
+        }
+        if (k >= 1) bar_sync(BAR_EMPTY0 + ((k - 1) & 1), OBS_THREADS);  // the last unit has been streamed
+        if (t == 0) {
+            __threadfence();
+            if (atomicAdd(&ticket[1], 1) == (int)gridDim.x - 1) {
+                ticket[0] = 0;
+                ticket[1] = 0;
+            }
+        }
+    }
 }
 
 }  // namespace jq

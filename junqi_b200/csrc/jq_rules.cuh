@@ -28,6 +28,7 @@ constexpr unsigned FULL = 0xffffffffu;
 // Device tables (filled by the host API, see jq_api.cu)
 // ---------------------------------------------------------------------------
 __constant__ Topo c_topo;
+__device__ Topo g_topo;  // same tables in global memory, for per-lane (divergent) reads
 __constant__ int64_t c_zturn[4], c_zwin[3], c_zsdead[4], c_zsflag[4], c_zshow[4];
 __constant__ int64_t c_zterm, c_zdraw;
 __device__ int64_t g_zpiece[NP * 14 * NC];
@@ -91,17 +92,17 @@ __device__ void warp_load(const jq_batch &b, const Topo &T, WEnv &w, int e, int 
 // ---------------------------------------------------------------------------
 // Destination mask of one piece standing on compact cell c (move_gen.py:
 // 1311-1553 restricted to one candidate piece).
-__device__ void piece_dsts(const Topo &T, int c, int t, const uint32_t *empty, const uint32_t *land,
-                           uint32_t *out) {
+__device__ void piece_dsts(const Topo &T, int c, int t, const uint32_t (&empty)[NW], const uint32_t (&land)[NW],
+                           uint32_t (&out)[NW]) {
 #pragma unroll
     for (int i = 0; i < NW; ++i) out[i] = 0;
     if (c < 0 || t == JUNQI || t == DILEI || (T.flags[c] & F_SH)) return;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
         int nb = T.adj4[c][k];
-        if (nb != NONE8 && mbit(land, nb)) mset(out, nb);
+        if (nb != NONE8 && rbit(land, nb)) rset(out, nb);
         nb = T.diag[c][k];
-        if (nb != NONE8 && mbit(land, nb)) mset(out, nb);
+        if (nb != NONE8 && rbit(land, nb)) rset(out, nb);
     }
     if (!(T.flags[c] & F_RAIL)) return;
     if (t == GONGB) {
@@ -109,8 +110,8 @@ __device__ void piece_dsts(const Topo &T, int c, int t, const uint32_t *empty, c
         uint32_t reach[NW], fr[NW], landing[NW];
 #pragma unroll
         for (int i = 0; i < NW; ++i) reach[i] = fr[i] = landing[i] = 0;
-        mset(reach, c);
-        mset(fr, c);
+        rset(reach, c);
+        rset(fr, c);
         for (int it = 0; it < NB; ++it) {
             uint32_t nbm[NW] = {0, 0, 0, 0, 0};
 #pragma unroll
@@ -134,7 +135,8 @@ __device__ void piece_dsts(const Topo &T, int c, int t, const uint32_t *empty, c
             }
             if (!any) break;
         }
-        landing[c >> 5] &= ~(1u << (c & 31));
+#pragma unroll
+        for (int i = 0; i < NW; ++i) landing[i] &= (c >> 5) == i ? ~(1u << (c & 31)) : ~0u;
 #pragma unroll
         for (int i = 0; i < NW; ++i) out[i] |= landing[i];
     } else {
@@ -142,16 +144,16 @@ __device__ void piece_dsts(const Topo &T, int c, int t, const uint32_t *empty, c
             for (int l = 0; l < 12; ++l) {
                 int nb = T.sray[c][k][l];
                 if (nb == NONE8) break;
-                if (mbit(land, nb)) mset(out, nb);
-                if (!mbit(empty, nb)) break;
+                if (rbit(land, nb)) rset(out, nb);
+                if (!rbit(empty, nb)) break;
             }
         if (T.flags[c] & F_CURVE_ACTIVE)
             for (int k = 0; k < 2; ++k)
                 for (int l = 0; l < 11; ++l) {
                     int nb = T.cray[c][k][l];
                     if (nb == NONE8) break;
-                    if (mbit(land, nb)) mset(out, nb);
-                    if (!mbit(empty, nb)) break;
+                    if (rbit(land, nb)) rset(out, nb);
+                    if (!rbit(empty, nb)) break;
                 }
     }
 }
@@ -186,6 +188,20 @@ __device__ bool warp_has_moves(const Topo &T, const WEnv &w, int lane, int seat)
     uint32_t empty[NW], land[NW], d[NW];
     board_masks(T, w, lane, seat & 1, empty, land);
     int src = lane_source(w, lane, seat);
+    // A one-step (orthogonal or camp-diagonal) move of a movable piece is a
+    // legal move on its own; only when no piece has one is the full
+    // destination set (rail rays, engineer flood-fill) needed.
+    bool quick = false;
+    if (src >= 0) {
+        const int t = w.type[seat * 30 + lane];
+        if (t != JUNQI && t != DILEI && !(T.flags[src] & F_SH))
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int a = T.adj4[src][k], g = T.diag[src][k];
+                quick |= (a != NONE8 && rbit(land, a)) || (g != NONE8 && rbit(land, g));
+            }
+    }
+    if (__any_sync(FULL, quick)) return true;
     bool any = false;
     if (src >= 0) {
         piece_dsts(T, src, w.type[seat * 30 + lane], empty, land, d);
@@ -194,16 +210,23 @@ __device__ bool warp_has_moves(const Topo &T, const WEnv &w, int lane, int seat)
     return __any_sync(FULL, any);
 }
 
-__device__ __forceinline__ uint4 mask_chunk(const WEnv &w, int j0) {
-    int row = j0 / NB, col = j0 - row * NB;
-    uint32_t v[4] = {0, 0, 0, 0};
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-        uint32_t bit = row < NB ? (w.canon[row][col >> 5] >> (col & 31)) & 1u : 0u;
-        v[i >> 2] |= bit << ((i & 3) * 8);
-        if (++col == NB) { col = 0; ++row; }
-    }
-    return make_uint4(v[0], v[1], v[2], v[3]);
+// n <= 16 bits of canonical row `row` starting at column col (0 past the row).
+__device__ __forceinline__ uint32_t row_bits(const WEnv &w, int row, int col, int n) {
+    if (row >= NB || n <= 0) return 0u;
+    const int wi = col >> 5;
+    const uint32_t lo = w.canon[row][wi], hi = wi + 1 < NW ? w.canon[row][wi + 1] : 0u;
+    return __funnelshift_r(lo, hi, col & 31) & ((1u << n) - 1u);
+}
+
+// 4 mask bits -> 4 bytes of 0/1 (bit i -> byte i).
+__device__ __forceinline__ uint32_t nibble_bytes(uint32_t nib) { return (nib * 0x00204081u) & 0x01010101u; }
+
+// 16 mask bytes starting at byte j0 = row * 129 + col of the canonical mask.
+__device__ __forceinline__ uint4 mask_chunk(const WEnv &w, int row, int col) {
+    const int n0 = NB - col < 16 ? NB - col : 16;
+    const uint32_t bits = row_bits(w, row, col, n0) | (row_bits(w, row + 1, 0, 16 - n0) << n0);
+    return make_uint4(nibble_bytes(bits & 15u), nibble_bytes((bits >> 4) & 15u), nibble_bytes((bits >> 8) & 15u),
+                      nibble_bytes(bits >> 12));
 }
 
 // Legal actions of `seat` (empty when `skip`), ascending, written to ids
@@ -256,6 +279,12 @@ __device__ int warp_legal(const Topo &T, WEnv &w, int lane, int seat, bool skip,
     }
     if (mask_env) {
         for (int k = lane; k < NB * NW; k += 32) (&w.canon[0][0])[k] = 0u;
+        // rows (canonical sources) that hold at least one destination
+        uint32_t rows[NW];
+        const int myrow = (src >= 0 && cnt > 0) ? T.rot[seat][src] : -1;
+#pragma unroll
+        for (int i = 0; i < NW; ++i)
+            rows[i] = __reduce_or_sync(FULL, (myrow >= 0 && (myrow >> 5) == i) ? (1u << (myrow & 31)) : 0u);
         __syncwarp();
         if (src >= 0) {
             uint32_t *row = w.canon[T.rot[seat][src]];
@@ -276,9 +305,17 @@ __device__ int warp_legal(const Topo &T, WEnv &w, int lane, int seat, bool skip,
             mask_env[j] = (uint8_t)((w.canon[row][col >> 5] >> (col & 31)) & 1u);
         }
         int body = (MASK_BYTES - head) >> 4;
+        // lane k writes chunks k, k + 32, ...: byte j0 = head + 16 k, advancing
+        // 512 bytes = 3 rows + 125 columns per step
+        int j0 = head + lane * 16;
+        int row = j0 / NB, col = j0 - row * NB;
         for (int k = lane; k < body; k += 32) {
-            int j0 = head + k * 16;
-            *reinterpret_cast<uint4 *>(mask_env + j0) = mask_chunk(w, j0);
+            const int row2 = col + 15 >= NB ? row + 1 : row;
+            const bool any = rbit(rows, row) || (row2 < NB && rbit(rows, row2));
+            *reinterpret_cast<uint4 *>(mask_env + head + k * 16) = any ? mask_chunk(w, row, col) : make_uint4(0u, 0u, 0u, 0u);
+            col += 512 - 3 * NB;
+            row += 3;
+            if (col >= NB) { col -= NB; ++row; }
         }
         for (int j = head + body * 16 + lane; j < MASK_BYTES; j += 32) {
             int row = j / NB, col = j - row * NB;
@@ -305,8 +342,8 @@ __device__ bool ray_clear_to(const Topo &T, const WEnv &w, const uint8_t *ray, i
 __device__ bool engineer_reach(const Topo &T, const WEnv &w, int s, int d) {
     if (!(T.flags[s] & F_RAIL) || !(T.flags[d] & F_RAIL) || s == d) return false;
     uint32_t reach[NW] = {0, 0, 0, 0, 0}, fr[NW] = {0, 0, 0, 0, 0};
-    mset(reach, s);
-    mset(fr, s);
+    rset(reach, s);
+    rset(fr, s);
     for (int it = 0; it < NB; ++it) {
         uint32_t nbm[NW] = {0, 0, 0, 0, 0};
         for (int wd = 0; wd < NW; ++wd) {
@@ -317,7 +354,7 @@ __device__ bool engineer_reach(const Topo &T, const WEnv &w, int s, int d) {
                 for (int i = 0; i < NW; ++i) nbm[i] |= T.railnb[v][i];
             }
         }
-        if (mbit(nbm, d)) return true;
+        if (rbit(nbm, d)) return true;
         uint32_t any = 0;
         for (int i = 0; i < NW; ++i) {
             uint32_t nw = nbm[i] & ~reach[i];
@@ -535,12 +572,27 @@ __device__ void warp_belief_update(const jq_batch &b, const Topo &T, const WEnv 
             if (died[s]) rem_untrack(b, e, o, s);
     }
     __syncwarp();
-    for (int k = lane; k < 4 * NP; k += 32) {
-        int o = k / NP, p = k - o * NP;
-        uint8_t *c = &b.bel_code[OI(e, o, p)];
-        if (!w.alive[p]) { *c = BC_NONE; continue; }
-        if (*c == BC_NONE)
-            *c = sees_truth(o, w.seat[p], mode) ? (uint8_t)(tracked_idx(w.type[p]) + 1) : (uint8_t)BC_UNIFORM;
+    // I5 sweep over the env's 4 x 120 codes, 16 per lane (rows are 480 bytes,
+    // 16-byte aligned: the host checks the base)
+    if (lane < 4 * NP / 16) {
+        uint4 *row = reinterpret_cast<uint4 *>(b.bel_code + OI(e, 0, 0)) + lane;
+        uint4 v = *row;
+        uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+        bool changed = false;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const int k = lane * 16 + i, o = k >= 3 * NP ? 3 : k >= 2 * NP ? 2 : k >= NP ? 1 : 0, p = k - o * NP;
+            const uint32_t c = (wv[i >> 2] >> ((i & 3) * 8)) & 0xFFu;
+            uint32_t nc = c;
+            if (!w.alive[p]) nc = BC_NONE;
+            else if (c == BC_NONE)
+                nc = sees_truth(o, w.seat[p], mode) ? (uint32_t)(tracked_idx(w.type[p]) + 1) : (uint32_t)BC_UNIFORM;
+            if (nc != c) {
+                changed = true;
+                wv[i >> 2] = (wv[i >> 2] & ~(0xFFu << ((i & 3) * 8))) | (nc << ((i & 3) * 8));
+            }
+        }
+        if (changed) *row = make_uint4(wv[0], wv[1], wv[2], wv[3]);
     }
     __syncwarp();
 }

@@ -318,6 +318,35 @@ class OracleBatch:
         return sp, gl
 
 
+def zobrist_recompute(a: dict[str, np.ndarray], show_mode: int) -> np.ndarray:
+    """Zobrist hash of every env rebuilt from scratch (state.py:1761-1815,
+    ``_recompute_zobrist``), vectorised over envs.  ``a`` holds the batch
+    fields (oracle names); returns int64 (N,)."""
+    z = zobrist_tables()
+    alive = np.asarray(a["alive"]).astype(bool)
+    n = alive.shape[0]
+    t = np.asarray(a["piece_type"]).astype(np.int64)
+    flat = np.asarray(a["pos_y"]).astype(np.int64) * 17 + np.asarray(a["pos_x"]).astype(np.int64)
+    live = alive & (t >= 0) & (flat >= 0)
+    pid = np.broadcast_to(np.arange(120), alive.shape)
+    keys = np.where(live, z["piece"][pid, np.clip(t, 0, 13), np.clip(flat, 0, 288)], 0).view(np.uint64)
+    h = np.bitwise_xor.reduce(keys, axis=1)
+    u = lambda x: np.asarray(x, np.int64).view(np.uint64)  # noqa: E731
+    h ^= u(z["turn"][np.asarray(a["turn"]).astype(np.int64) & 3])
+    h ^= u(z["mc"][np.asarray(a["move_counter"]).astype(np.int64) & 0xFFF])
+    h ^= u(z["mslc"][np.asarray(a["mslc"]).astype(np.int64) & 0x1FF])
+    h ^= u(z["winner"][np.asarray(a["winner"]).astype(np.int64) + 1])
+    h ^= u(np.full(n, z["show_mode"][show_mode]))
+    h ^= np.where(np.asarray(a["terminated"]).astype(bool), u(z["terminated"][0]), np.uint64(0))
+    h ^= np.where(np.asarray(a["draw"]).astype(bool), u(z["draw"][0]), np.uint64(0))
+    sd = np.asarray(a["seat_dead"]).astype(bool).reshape(n, 4)
+    sf = np.asarray(a["seat_flag"]).astype(bool).reshape(n, 4)
+    for s in range(4):
+        h ^= np.where(sd[:, s], u(z["seat_dead"][s]), np.uint64(0))
+        h ^= np.where(sf[:, s], u(z["seat_flag"][s]), np.uint64(0))
+    return h.view(np.int64)
+
+
 def load_state(batch: OracleBatch, arrays: dict[str, np.ndarray], init_beliefs: bool = True) -> None:
     """Copy state fields (oracle names) into ``batch`` and seed beliefs."""
     for k, v in arrays.items():

@@ -74,3 +74,13 @@ def test_oracle_replays_reference_trajectory(name):
     fx = G.load(name)
     n = G.replay(fx, OracleDriver())
     assert n == fx["actions"].shape[0]
+
+
+@pytest.mark.parametrize("name", G.TRAJECTORIES)
+def test_zobrist_recompute_matches_reference_hashes(name):
+    """The vectorised from-scratch hash (state.py:1761) equals the reference's
+    incremental hash on the initial and final states of every trajectory."""
+    fx = G.load(name)
+    for pre in ("init_", "final_"):
+        st = {k[len(pre):]: v for k, v in fx.items() if k.startswith(pre)}
+        assert np.array_equal(O.zobrist_recompute(st, int(fx["show_mode"])), st["zobrist"].astype(np.int64)), pre
