@@ -177,22 +177,45 @@ __device__ void stage_piece(const jq_batch &b, int e, int o, int mode, const Obs
     const int mcnt = b.move_count[q], ae_raw = b.active_eat[q], ps_raw = b.passive_surv[q];
     const int dstep = b.death_step[q], dreason = b.death_reason[q], dloc = b.death_loc[q];
     const int code = b.bel_code[k];
-    const uint64_t dlo = b.cm_direct_lo[k], dhi = b.cm_direct_hi[k];
-    const uint64_t clo = b.cm_chain_lo[k], chi = b.cm_chain_hi[k];
-    const uint64_t elo = b.cm_eaten_lo[k], ehi = b.cm_eaten_hi[k];
-    const int dtype = b.cm_direct_type[k], ctype = b.cm_chain_type[k];
-    const int other = b.cm_direct_other[k], fl = b.cm_rank_floor[k];
-    const int is_g = b.cm_is_gongb[k], not_g = b.cm_not_gongb[k], atk_g = b.cm_atk_gongb[k];
-    const int last_d = b.cm_last_direct_step[k], last_c = b.cm_last_chain_step[k], last_f = b.cm_rank_floor_step[k];
+    // an alive piece's seat is its pid / 30, so whether the observer sees it
+    // as an enemy (and needs its combat-memory row) is known before any load
+    const bool enemy_pid = ((p / 30) & 1) != oteam;
+    uint64_t dlo = 0, dhi = 0, clo = 0, chi = 0;
+    int dtype = 0, ctype = 0, other = 0, fl = 0, is_g = 0, not_g = 0, atk_g = 0, last_d = -1, last_c = -1, last_f = -1;
+    if (enemy_pid) {
+        dlo = b.cm_direct_lo[k];
+        dhi = b.cm_direct_hi[k];
+        clo = b.cm_chain_lo[k];
+        chi = b.cm_chain_hi[k];
+        dtype = b.cm_direct_type[k];
+        ctype = b.cm_chain_type[k];
+        other = b.cm_direct_other[k];
+        fl = b.cm_rank_floor[k];
+        is_g = b.cm_is_gongb[k];
+        not_g = b.cm_not_gongb[k];
+        atk_g = b.cm_atk_gongb[k];
+        last_d = b.cm_last_direct_step[k];
+        last_c = b.cm_last_chain_step[k];
+        last_f = b.cm_rank_floor_step[k];
+    }
     const int cur = b.move_counter[e];
-    const size_t kl = OI(e, left, p), kr = OI(e, right, p);
-    const int lc = __popcll(b.cm_direct_lo[kl]) + __popcll(b.cm_direct_hi[kl]) + b.cm_direct_other[kl];
-    const int rc = __popcll(b.cm_direct_lo[kr]) + __popcll(b.cm_direct_hi[kr]) + b.cm_direct_other[kr];
-    const int lg = b.cm_is_gongb[kl] && b.cm_is_gongb[kr];
-    const bool patk = b.cm_atk_gongb[kl] || b.cm_atk_gongb[kr];
+    // the observer's own pieces (pids o*30 .. o*30+29, one warp-aligned group
+    // of lanes) also read the opponents' view of them and their eaten-by sets
+    const bool own_pid = (p / 30) == o;
+    int lc = 0, rc = 0, lg = 0;
+    bool patk = false;
+    uint64_t elo = 0, ehi = 0;
+    if (own_pid) {
+        const size_t kl = OI(e, left, p), kr = OI(e, right, p);
+        lc = __popcll(b.cm_direct_lo[kl]) + __popcll(b.cm_direct_hi[kl]) + b.cm_direct_other[kl];
+        rc = __popcll(b.cm_direct_lo[kr]) + __popcll(b.cm_direct_hi[kr]) + b.cm_direct_other[kr];
+        lg = b.cm_is_gongb[kl] && b.cm_is_gongb[kr];
+        patk = b.cm_atk_gongb[kl] || b.cm_atk_gongb[kr];
+        elo = b.cm_eaten_lo[k];
+        ehi = b.cm_eaten_hi[k];
+    }
 
     const int team = s >= 0 ? (s & 1) : 1;  // numpy _SEAT_TEAM[-1] is EAST's team
-    const bool own_pid = (p / 30) == o;
     int cell;
     if (alive_raw) {
         if (!(x >= 0 && x < 17 && y >= 0 && y < 17)) return;
