@@ -41,6 +41,9 @@ CONFIGS = {
     "cfg4": dict(envs=32768, seats=1, policy="softmax", pool=8192, plies=512, mode=2,
                  workload="configs[3]: 32768 envs/GPU, 512-ply rollout, pool of 8192, masked softmax, "
                           "episode stats all-reduced once per rollout"),
+    "cfg5": dict(envs=32768, seats=1, policy="uniform", pool=10_000, plies=2000, mode=2, start="late",
+                 workload="configs[4]: 32768 envs/GPU late-game starts (seeded setups, 0-60% of pieces removed, "
+                          "engineers on the railway), 2000 plies, uniform-random legal policy"),
 }
 
 OBS_WRITE = 317 * 289 * 4 + 28 * 4  # bytes written per (env, seat) observation
@@ -138,7 +141,8 @@ def profiled_traffic(cfg: str) -> float | None:
 # CPU arms (oracle = CPU restatement of the reference rules)
 # ---------------------------------------------------------------------------
 
-def cpu_rollout(envs: int, plies: int, seats: int, seed: int, threads: int, budget_s: float, rules: int = 1):
+def cpu_rollout(envs: int, plies: int, seats: int, seed: int, threads: int, budget_s: float, rules: int = 1,
+                late: bool = False):
     """Step + legal + observation on the CPU oracle; returns (plies/s, plies, seconds, sample text)."""
     os.environ["JQ_ORACLE_THREADS"] = str(threads)
     from junqi_b200 import tables
@@ -149,6 +153,10 @@ def cpu_rollout(envs: int, plies: int, seats: int, seed: int, threads: int, budg
     rng = np.random.default_rng(seed)
     for e in range(envs):
         b.reset_env(e, pool[e % len(pool)])
+    if late:  # the same host edit the GPU arm applies (junqi_b200/workloads.py)
+        from junqi_b200 import workloads
+        O.load_state(b, workloads.thin_positions({k: v.copy() for k, v in b.a.items()}, seed), init_beliefs=True)
+        b.a["zobrist"][:] = O.zobrist_recompute(b.a, 2)
     done = 0
     t0 = time.perf_counter()
     t = 0
@@ -191,7 +199,7 @@ def reference_arm(args, cfg: dict) -> None:
     for _ in range(args.warmup if args.warmup < 3 else 2):
         cpu_rollout(min(envs, 64), 1, cfg["seats"], args.seed, threads, 5.0, RULES[args.rules])
     rate, done, dt, sample = cpu_rollout(envs, args.steps, cfg["seats"], args.seed, threads, 120.0,
-                                         RULES[args.rules])
+                                         RULES[args.rules], late=cfg.get("start") == "late")
     line = {"impl": "reference", "metric": "env plies/s (step + legal mask + 317-ch obs)", "value": rate,
             "unit": "plies/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8/int16/f32",
@@ -241,7 +249,8 @@ def main() -> None:
     torch.cuda.set_device(local)
     if world > 1:
         import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
 
     from junqi_b200 import _native
     from junqi_b200 import sharding
@@ -255,7 +264,11 @@ def main() -> None:
     env = JunqiEnvB200(n, device=local, show_mode=cfg["mode"], pool=pool, obs_seats=seats,
                        rules=RULES[args.rules])
     sampler = env.sample_uniform if cfg["policy"] == "uniform" else env.sample_softmax
-    env.reset(seed=seed)
+    if cfg.get("start") == "late":
+        from junqi_b200 import workloads
+        workloads.late_game_starts(env, seed)
+    else:
+        env.reset(seed=seed)
     stream = torch.cuda.current_stream()
 
     def one_ply(t, ev=None):
@@ -350,7 +363,7 @@ def main() -> None:
         if not args.no_cpu_baseline:
             threads = host_cores()
             rate, done, dt, sample = cpu_rollout(min(n, 64 * threads), 400, seats, args.seed, threads, 15.0,
-                                                 RULES[args.rules])
+                                                 RULES[args.rules], late=cfg.get("start") == "late")
             line["cpu_baseline"] = {"value": rate, "unit": "plies/s", "cores": threads, "kind": "port",
                                     "sample": sample + f", {dt:.1f} s"}
         print(json.dumps(line), flush=True)
@@ -379,6 +392,9 @@ def run_e2e(env, args, seed, stream) -> dict:
     steps = args.e2e_steps
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
+    import torch.distributed as dist
+    if dist.is_initialized():
+        dist.barrier()
     start.record(stream)
     for t in range(steps):
         o = off_h.numpy()
@@ -402,7 +418,9 @@ def run_e2e(env, args, seed, stream) -> dict:
         applied += int(res_h["valid"].numpy().sum())
     end.record(stream)
     torch.cuda.synchronize()
-    ms = start.elapsed_time(end)
+    from junqi_b200 import sharding
+    ms = sharding.max_over_ranks(start.elapsed_time(end), env.device)
+    applied = sharding.sum_over_ranks(applied, env.device)
     return {"value": applied / (ms / 1e3), "unit": "plies/s", "h2d_bytes_per_step": h2d // steps,
             "d2h_bytes_per_step": d2h // steps, "steps": steps,
             "api": "JunqiEnvB200.ply/observe/csr with pinned host actions in, MoveResult + CSR out"}
