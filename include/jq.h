@@ -162,6 +162,17 @@ int jq_reset(const jq_batch *b, uint64_t seed, uint64_t ply, int32_t all, int32_
  * (bindings.cpp:1262-1270). */
 int jq_init_beliefs(const jq_batch *b, int32_t show_mode, void *stream);
 
+/* Per-piece 80-slot legal mask of each env's seat (d_seats (N,) int8, or
+ * NULL for the env's turn): d_slots is (N, 120, 80) uint8, 16-byte aligned,
+ * 1 where piece pid can make the move of that slot -- slots 0..3 orthogonal
+ * one-steps (+x, -x, +y, -y), 4..7 camp diagonals, 8..55 straight rail ray d
+ * cell k at 8 + 12 d + k, 56..67 curve-rail cells off the source's row and
+ * column in breadth-first order, and for engineers 8..79 the rail cells
+ * reachable through empty rail in breadth-first order (orthogonal
+ * neighbours excluded).  Replaces legal_action_mask_batch
+ * (bindings.cpp:951-1000, game_state.cu:1985-2197). */
+int jq_legal_slots(const jq_batch *b, const int8_t *d_seats, uint8_t *d_slots, void *stream);
+
 /* Rebuild every env's Zobrist hash from its state, for state written by the
  * caller (a position built on the host).  Device counterpart of the
  * reference's host-side _recompute_zobrist (state.py:1761-1815), which

@@ -69,6 +69,7 @@ SIGNATURES = {
     "jq_reset": (ctypes.c_int, [_PB, _u64, _u64, _i32, _i32, _vp]),
     "jq_init_beliefs": (ctypes.c_int, [_PB, _i32, _vp]),
     "jq_rehash": (ctypes.c_int, [_PB, _i32, _vp]),
+    "jq_legal_slots": (ctypes.c_int, [_PB, _vp, _vp, _vp]),
     "jq_step": (ctypes.c_int, [_PB, _vp, _i32, _PO, _vp]),
     "jq_step_canonical": (ctypes.c_int, [_PB, _vp, _vp, _i32, _PO, _vp]),
     "jq_ply": (ctypes.c_int, [_PB, _vp, _i32, _PO, _i32, _u64, _u64, _vp, _vp, _i32, _vp, _vp, _vp]),

@@ -58,6 +58,17 @@ struct __align__(16) Topo {
     int8_t slot_ch[30];        // piece-slot channel of a seat-local slot, -1 camp
 };
 
+// Tables of the per-piece 80-slot legal mask (the reference GPU format of
+// legal_action_mask_batch): flat-space neighbours in the order that format
+// numbers its slots, and the rail graph in rail-index space (rail cells in
+// flat order, neighbours ascending).
+struct __align__(16) SlotTopo {
+    int16_t adj8[NC][8];   // 0..3 orthogonal (+x, -x, +y, -y), 4..7 camp diagonals compacted; -1 none
+    int16_t rcell[80];     // rail index -> flat
+    int8_t ri[NC];         // flat -> rail index, -1 off the railway
+    int8_t rn[80][8];      // rail-index neighbours, ascending, -1 padded
+};
+
 __host__ __device__ inline int tracked_idx(int t) { return (t >= 2 && t <= 13) ? t - 2 : -1; }
 __host__ __device__ inline bool is_ranked(int t) { return t >= SILING && t <= GONGB; }
 __host__ __device__ inline int team_of_pid(int pid) { return (pid / 30) & 1; }

@@ -13,6 +13,7 @@
 
 #include "jq_obs.cuh"
 #include "jq_rules.cuh"
+#include "jq_slots.cuh"
 #include "jq_topo_build.h"
 
 namespace jq {
@@ -367,10 +368,16 @@ int jq_init(int device) {
     DeviceState &st = g_dev[device];
     if (st.topo) return JQ_OK;
     static Topo host_topo;
+    static SlotTopo host_slot;
     static bool built = false;
-    if (!built) { build_topo(host_topo); built = true; }
+    if (!built) {
+        build_topo(host_topo);
+        build_slot_topo(host_topo, host_slot);
+        built = true;
+    }
     CU(cudaMemcpyToSymbol(c_topo, &host_topo, sizeof(Topo)));
     CU(cudaMemcpyToSymbol(g_topo, &host_topo, sizeof(Topo)));
+    CU(cudaMemcpyToSymbol(g_slot, &host_slot, sizeof(SlotTopo)));
     CU(cudaFuncSetAttribute(rules_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rule_smem()));
     CU(cudaFuncSetAttribute(obs_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)obs_smem()));
     CU(cudaDeviceGetAttribute(&st.sms, cudaDevAttrMultiProcessorCount, device));
@@ -466,6 +473,21 @@ int jq_init_beliefs(const jq_batch *b, int32_t show_mode, void *stream) {
     if (rc) return rc;
     a.flags = DO_BELIEF_INIT;
     return launch_rules(a, (cudaStream_t)stream);
+}
+
+int jq_legal_slots(const jq_batch *b, const int8_t *d_seats, uint8_t *d_slots, void *stream) {
+    int rc = check_batch(b);
+    if (rc) return rc;
+    if (!d_slots) return fail(JQ_ERR_ARG, "slot mask output missing");
+    if ((uintptr_t)d_slots & 15) return fail(JQ_ERR_ARG, "slot mask output must be 16-byte aligned");
+    DeviceState *st;
+    rc = current_dev(st);
+    if (rc) return rc;
+    if (!st->topo) return fail(JQ_ERR_NOT_READY, "jq_init was not called on this device");
+    const size_t threads = (size_t)b->n * NP;
+    slot_mask_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, (cudaStream_t)stream>>>(*b, d_seats, d_slots);
+    CU(cudaGetLastError());
+    return JQ_OK;
 }
 
 int jq_rehash(const jq_batch *b, int32_t show_mode, void *stream) {

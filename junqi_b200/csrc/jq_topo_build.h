@@ -179,4 +179,41 @@ inline void build_topo(Topo &T) {
     }
 }
 
+// The 80-slot mask's tables, derived from the compact tables above in the
+// order that format numbers its slots (tables.cu:176-211, 240-297 of the
+// reference CUDA extension).
+inline void build_slot_topo(const Topo &T, SlotTopo &S) {
+    std::memset(&S, 0xff, sizeof S);  // -1 everywhere
+    auto on = [&](int f) { return T.f2c[f] >= 0; };
+    auto camp = [&](int f) { return T.f2c[f] >= 0 && (T.flags[T.f2c[f]] & F_CAMP); };
+    const int od[4][2] = {{1, 0}, {-1, 0}, {0, 1}, {0, -1}}, dd[4][2] = {{1, 1}, {1, -1}, {-1, 1}, {-1, -1}};
+    for (int f = 0; f < NC; ++f) {
+        if (!on(f)) continue;
+        const int x = f % 17, y = f / 17;
+        for (int k = 0; k < 4; ++k) {
+            const int nx = x + od[k][0], ny = y + od[k][1];
+            if (nx >= 0 && nx < 17 && ny >= 0 && ny < 17 && on(ny * 17 + nx)) S.adj8[f][k] = (int16_t)(ny * 17 + nx);
+        }
+        int slot = 4;
+        for (int k = 0; k < 4; ++k) {
+            const int nx = x + dd[k][0], ny = y + dd[k][1];
+            if (nx < 0 || nx >= 17 || ny < 0 || ny >= 17) continue;
+            const int g = ny * 17 + nx;
+            if (on(g) && (camp(f) || camp(g))) S.adj8[f][slot++] = (int16_t)g;
+        }
+    }
+    int n = 0;
+    for (int f = 0; f < NC; ++f)
+        if (on(f) && (T.flags[T.f2c[f]] & F_RAIL)) {
+            S.ri[f] = (int8_t)n;
+            S.rcell[n++] = (int16_t)f;
+        }
+    for (int r = 0; r < n; ++r) {
+        const int c = T.f2c[S.rcell[r]];
+        int k = 0;
+        for (int v = 0; v < NB && k < 8; ++v)  // compact order is flat order, so this is ascending
+            if ((T.railnb[c][v >> 5] >> (v & 31)) & 1u) S.rn[r][k++] = S.ri[T.c2f[v]];
+    }
+}
+
 }  // namespace jq

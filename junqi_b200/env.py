@@ -136,6 +136,14 @@ class JunqiEnvB200:
                                  _stream_ptr()), "jq_legal")
         return self.counts, self.ids
 
+    def legal_slots(self, seats: torch.Tensor | None = None) -> torch.Tensor:
+        """Per-piece 80-slot legal mask (N, 120, 80) uint8 of each env's turn (or `seats`)."""
+        s = None if seats is None else seats.to(device=self.device, dtype=torch.int8).contiguous()
+        out = torch.empty((self.n, 120, 80), dtype=torch.uint8, device=self.device)
+        N.check(N.lib().jq_legal_slots(ctypes.byref(self.batch.struct), self._ptr(s), out.data_ptr(),
+                                       _stream_ptr()), "jq_legal_slots")
+        return out
+
     def csr(self):
         """(offsets (N+1,), values (N*cap,)) of the last legal generation."""
         N.check(N.lib().jq_csr(self.n, self.counts.data_ptr(), self.ids.data_ptr(), self.cap,

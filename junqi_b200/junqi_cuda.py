@@ -357,9 +357,13 @@ def legal_action_ids_batch_csr(state: DeviceGameStateBatch, acting_seats):
     return off, state._values[: int(off[-1])].cpu().numpy()
 
 
-def legal_action_mask_batch(state, acting_seats):
-    raise RuntimeError("legal_action_mask_batch (per-piece 80-slot mask) is not provided; "
-                       "use legal_mask_canonical_batch or the CSR")
+def legal_action_mask_batch(state: DeviceGameStateBatch, acting_seats) -> np.ndarray:
+    """bindings.cpp:951-1000: per-piece 80-slot mask, (N, 120, 80) bool on the host."""
+    s = _seats_dev(state, acting_seats)
+    out = torch.empty((state.num_envs, NUM_PIECES, SLOTS_PER_PIECE), dtype=torch.uint8, device=state.b.device)
+    N.check(N.lib().jq_legal_slots(ctypes.byref(state.struct), s.data_ptr(), out.data_ptr(), _stream()),
+            "jq_legal_slots")
+    return out.cpu().numpy().astype(bool)
 
 
 def legal_mask_canonical_batch(state: DeviceGameStateBatch, acting_seats) -> int:

@@ -435,6 +435,198 @@ int jqo_canonical_mask(const int32_t *ids, int count, int seat, uint8_t *mask) {
 }
 
 /* ======================================================================
+ * Per-piece 80-slot legal mask: the reference GPU format of
+ * legal_action_mask_batch (src/env/cuda/src/game_state.cu:1985-2197, tables
+ * from tables.cu:176-350).  junqi_core has no counterpart; this restates the
+ * kernel's algorithm so the CUDA path has a checker, and additionally
+ * reports the destination cell of every set slot.
+ * ====================================================================== */
+static int S_adj8[NC][8];      /* tables.cu:176-211: 4 ortho (+x,-x,+y,-y), then camp diagonals compacted */
+static int S_ri[NC];           /* flat -> rail index (rail cells in flat order) */
+static int S_rcell[NC];        /* rail index -> flat */
+static int S_nrail;
+static int S_rn[NC][8], S_nrn[NC]; /* rail-index adjacency, ascending (tables.cu:291) */
+static int S_sray[NC][4][12];  /* tables.cu:303-350 straight rays, -1 padded */
+static int S_ready = 0;
+
+static void build_slot_tables(void) {
+    if (S_ready) return;
+    build_topology();
+    static const int dd[4][2] = {{1, 1}, {1, -1}, {-1, 1}, {-1, -1}};
+    for (int f = 0; f < NC; ++f) {
+        for (int k = 0; k < 8; ++k) S_adj8[f][k] = -1;
+        if (!T_on[f]) continue;
+        for (int k = 0; k < 4; ++k) S_adj8[f][k] = T_adj[f][k];
+        int fx = f % 17, fy = f / 17, slot = 4;
+        for (int k = 0; k < 4 && slot < 8; ++k) {
+            int nx = fx + dd[k][0], ny = fy + dd[k][1];
+            if (nx < 0 || nx > 16 || ny < 0 || ny > 16) continue;
+            int g = ny * 17 + nx;
+            if (!T_on[g]) continue;
+            if (T_camp[f] || T_camp[g]) S_adj8[f][slot++] = g;
+        }
+    }
+    S_nrail = 0;
+    for (int f = 0; f < NC; ++f) {
+        S_ri[f] = -1;
+        if (T_rail[f]) { S_ri[f] = S_nrail; S_rcell[S_nrail++] = f; }
+    }
+    for (int r = 0; r < S_nrail; ++r) {
+        int f = S_rcell[r];
+        S_nrn[r] = 0;
+        for (int k = 0; k < T_nradj[f] && S_nrn[r] < 8; ++k) S_rn[r][S_nrn[r]++] = S_ri[T_radj[f][k]];
+    }
+    static const int d4[4][2] = {{1, 0}, {-1, 0}, {0, 1}, {0, -1}};
+    for (int f = 0; f < NC; ++f)
+        for (int d = 0; d < 4; ++d)
+            for (int k = 0; k < 12; ++k) S_sray[f][d][k] = -1;
+    for (int r = 0; r < S_nrail; ++r) {
+        int src = S_rcell[r], sx = src % 17, sy = src / 17;
+        for (int d = 0; d < 4; ++d) {
+            int k = 0, cur = src, prev = -1;
+            while (k < 12) {
+                int cr = S_ri[cur], next = -1;
+                if (cr < 0) break;
+                for (int i = 0; i < S_nrn[cr]; ++i) {
+                    int nb = S_rcell[S_rn[cr][i]];
+                    if (nb == prev) continue;
+                    int nx = nb % 17, ny = nb / 17;
+                    if (d4[d][0] != 0) {
+                        if (ny != sy || (nx - cur % 17) * d4[d][0] <= 0) continue;
+                    } else {
+                        if (nx != sx || (ny - cur / 17) * d4[d][1] <= 0) continue;
+                    }
+                    next = nb;
+                    break; /* the chain is simple: first match wins */
+                }
+                if (next < 0) break;
+                S_sray[src][d][k++] = next;
+                prev = cur;
+                cur = next;
+            }
+        }
+    }
+    S_ready = 1;
+}
+
+int jqo_slot_tables(int32_t *adj8 /*289x8*/, int32_t *srays /*289x4x12*/, int32_t *rail_adj /*289x8 flat*/) {
+    build_slot_tables();
+    for (int f = 0; f < NC; ++f) {
+        for (int k = 0; k < 8; ++k) {
+            adj8[f * 8 + k] = S_adj8[f][k];
+            rail_adj[f * 8 + k] = (S_ri[f] >= 0 && k < S_nrn[S_ri[f]]) ? S_rcell[S_rn[S_ri[f]][k]] : -1;
+        }
+        for (int d = 0; d < 4; ++d)
+            for (int k = 0; k < 12; ++k) srays[(f * 4 + d) * 12 + k] = S_sray[f][d][k];
+    }
+    return 0;
+}
+
+/* game_state.cu:1985-2197, one (env, pid) row per piece of `seat`. */
+int jqo_slot_mask(const jqo_batch *b, int env, int seat, uint8_t *mask /*120x80*/, int16_t *dst /*120x80*/) {
+    build_slot_tables();
+    memset(mask, 0, NP * JQO_SLOTS);
+    if (dst)
+        for (int i = 0; i < NP * JQO_SLOTS; ++i) dst[i] = -1;
+    const size_t q0 = (size_t)env * NP;
+    const int16_t *cp = b->cell_pid + (size_t)env * NC;
+    const int team = seat & 1;
+#define SLOT_SET(slot, cell)                                    \
+    do {                                                        \
+        mask[pid * JQO_SLOTS + (slot)] = 1;                     \
+        if (dst) dst[pid * JQO_SLOTS + (slot)] = (int16_t)(cell); \
+    } while (0)
+    for (int pid = 0; pid < NP; ++pid) {
+        if (b->piece_seat[q0 + pid] != seat || !b->alive[q0 + pid]) continue;
+        int t = b->piece_type[q0 + pid];
+        if (t == T_JUNQI || t == T_DILEI) continue;
+        int sx = b->pos_x[q0 + pid], sy = b->pos_y[q0 + pid];
+        if (sx < 0 || sy < 0) continue;
+        int src = sy * 17 + sx;
+        if (src >= NC || !T_on[src] || T_sh[src]) continue;
+#define ENEMY_AT(cell, occ) ((((int)b->piece_seat[q0 + (occ)]) & 1) != team && !T_camp[cell])
+        for (int k = 0; k < 8; ++k) {
+            int nb = S_adj8[src][k];
+            if (nb < 0) continue;
+            int occ = cp[nb];
+            if (occ < 0 || ENEMY_AT(nb, occ)) SLOT_SET(k, nb);
+        }
+        if (!T_rail[src]) continue;
+        const int o0 = S_adj8[src][0], o1 = S_adj8[src][1], o2 = S_adj8[src][2], o3 = S_adj8[src][3];
+#define IS_ORTHO(c) ((c) == o0 || (c) == o1 || (c) == o2 || (c) == o3)
+        unsigned char vis[NC];
+        int qu[NC], qh = 0, qt = 0;
+        if (t != T_GONGB) {
+            for (int d = 0; d < 4; ++d)
+                for (int k = 0; k < 12; ++k) {
+                    int nb = S_sray[src][d][k];
+                    if (nb < 0) break;
+                    int occ = cp[nb], slot = 8 + d * 12 + k;
+                    if (occ < 0) {
+                        if (!IS_ORTHO(nb)) SLOT_SET(slot, nb);
+                    } else {
+                        if (!IS_ORTHO(nb) && ENEMY_AT(nb, occ)) SLOT_SET(slot, nb);
+                        break;
+                    }
+                }
+            int sc = T_curve[src], sr = S_ri[src];
+            if (sc > 0 && sr >= 0) {
+                memset(vis, 0, sizeof vis);
+                vis[sr] = 1;
+                qu[qt++] = sr;
+                int cs = 56;
+                while (qh < qt) {
+                    int cur = qu[qh++];
+                    for (int i = 0; i < S_nrn[cur]; ++i) {
+                        int nr = S_rn[cur][i];
+                        if (vis[nr]) continue;
+                        vis[nr] = 1;
+                        int nf = S_rcell[nr];
+                        if (T_curve[nf] != sc) continue;
+                        int same_axis = (nf % 17 == sx) || (nf / 17 == sy);
+                        int occ = cp[nf];
+                        if (occ < 0) {
+                            if (!same_axis && cs < 68) { SLOT_SET(cs, nf); ++cs; }
+                            qu[qt++] = nr;
+                        } else if (!same_axis && cs < 68 && ENEMY_AT(nf, occ)) {
+                            SLOT_SET(cs, nf);
+                            ++cs;
+                        }
+                    }
+                }
+            }
+        } else {
+            int sr = S_ri[src];
+            if (sr < 0) continue;
+            memset(vis, 0, sizeof vis);
+            vis[sr] = 1;
+            qu[qt++] = sr;
+            int cs = 8;
+            while (qh < qt) {
+                int cur = qu[qh++];
+                for (int i = 0; i < S_nrn[cur]; ++i) {
+                    int nr = S_rn[cur][i];
+                    if (vis[nr]) continue;
+                    vis[nr] = 1;
+                    int nf = S_rcell[nr], occ = cp[nf];
+                    if (occ < 0) {
+                        if (!IS_ORTHO(nf) && cs < JQO_SLOTS) { SLOT_SET(cs, nf); ++cs; }
+                        qu[qt++] = nr;
+                    } else if (!IS_ORTHO(nf) && cs < JQO_SLOTS && ENEMY_AT(nf, occ)) {
+                        SLOT_SET(cs, nf);
+                        ++cs;
+                    }
+                }
+            }
+        }
+#undef IS_ORTHO
+#undef ENEMY_AT
+    }
+#undef SLOT_SET
+    return 0;
+}
+
+/* ======================================================================
  * move_requires_gongb (move_gen.py:245-296) on the pre-move board
  * ====================================================================== */
 /* move_gen.py:127-165 _straight_rail_clear */

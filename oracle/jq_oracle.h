@@ -105,6 +105,9 @@ int jqo_legal(const jqo_batch *b, int env, int seat, int ignore_skip, int32_t *o
 int jqo_legal_batch(const jqo_batch *b, const int8_t *seats, int32_t *counts,
                     int32_t *ids /* n x cap */, int cap, int nthreads);
 int jqo_canonical_mask(const int32_t *ids, int count, int seat, uint8_t *mask16641);
+#define JQO_SLOTS 80
+int jqo_slot_tables(int32_t *adj8 /*289x8*/, int32_t *srays /*289x4x12*/, int32_t *rail_adj /*289x8*/);
+int jqo_slot_mask(const jqo_batch *b, int env, int seat, uint8_t *mask /*120x80*/, int16_t *dst /*120x80, or NULL*/);
 int jqo_obs(const jqo_batch *b, int env, int observer, int show_mode, float *spatial,
             float *global);
 int jqo_obs_batch(const jqo_batch *b, const int8_t *observers, int show_mode,

@@ -301,6 +301,18 @@ class OracleBatch:
                                  _ptr(m, ctypes.c_uint8))
         return m.astype(bool)
 
+    def slot_mask(self, seats: np.ndarray | None = None) -> tuple[np.ndarray, np.ndarray]:
+        """Per-piece 80-slot legal mask of the reference GPU format
+        (game_state.cu:1985-2197): (n, 120, 80) bool and the destination flat
+        cell of every set slot (n, 120, 80) int16, -1 elsewhere."""
+        seats = self["turn"] if seats is None else np.asarray(seats, np.int8)
+        mask = np.zeros((self.n, 120, 80), np.uint8)
+        dst = np.zeros((self.n, 120, 80), np.int16)
+        for e in range(self.n):
+            lib().jqo_slot_mask(ctypes.byref(self._c), e, int(seats[e]), _ptr(mask[e], ctypes.c_uint8),
+                                _ptr(dst[e], ctypes.c_int16))
+        return mask.astype(bool), dst
+
     def obs(self, observers: np.ndarray | None = None):
         """(n, 317, 17, 17) float32 + (n, 28) float32 for one observer per env."""
         obsv = self.a["turn"] if observers is None else np.ascontiguousarray(observers, dtype=np.int8)
@@ -345,6 +357,15 @@ def zobrist_recompute(a: dict[str, np.ndarray], show_mode: int) -> np.ndarray:
         h ^= np.where(sd[:, s], u(z["seat_dead"][s]), np.uint64(0))
         h ^= np.where(sf[:, s], u(z["seat_flag"][s]), np.uint64(0))
     return h.view(np.int64)
+
+
+def slot_tables() -> dict[str, np.ndarray]:
+    """The 80-slot mask's tables as the oracle rebuilds them (tables.cu:176-350)."""
+    adj8 = np.zeros((289, 8), np.int32)
+    sr = np.zeros((289, 4, 12), np.int32)
+    ra = np.zeros((289, 8), np.int32)
+    lib().jqo_slot_tables(_ptr(adj8, ctypes.c_int32), _ptr(sr, ctypes.c_int32), _ptr(ra, ctypes.c_int32))
+    return {"adj8": adj8, "srays": sr, "rail_adj": ra}
 
 
 def load_state(batch: OracleBatch, arrays: dict[str, np.ndarray], init_beliefs: bool = True) -> None:

@@ -124,3 +124,19 @@ def test_step_device_pointer_dict():
     d = jc.step_device(state, acts.data_ptr(), turn.data_ptr())
     assert d["N"] == n and all(isinstance(v, int) for v in d.values())
     assert not state._out["valid"].any()
+
+
+def test_legal_action_mask_batch_is_the_80_slot_mask():
+    _setup()
+    n = 12
+    pool = tables.build_setup_pool(n, seed=41)
+    orc = O.OracleBatch(n, 2)
+    for e in range(n):
+        orc.reset_env(e, pool[e])
+    state = jc.DeviceGameStateBatch(n)
+    state.copy_from_host(_pack(orc))
+    seats = orc["turn"].copy()
+    m = jc.legal_action_mask_batch(state, seats)
+    assert m.shape == (n, 120, 80) and m.dtype == bool
+    exp, _ = orc.slot_mask(seats)
+    assert np.array_equal(m, exp)

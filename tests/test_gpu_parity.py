@@ -212,3 +212,28 @@ def test_status_codes_surface_as_errors():
     assert st == 1
     with pytest.raises(RuntimeError, match="JQ_ERR_ARG"):
         N.check(L.jq_legal(ctypes.byref(env.batch.struct), None, None, None, 0, None, None), "jq_legal")
+
+
+@pytest.mark.parametrize("late", [False, True])
+def test_slot_mask_matches_oracle(late):
+    """jq_legal_slots (per-piece 80-slot mask) against the oracle restatement,
+    including late-game positions with engineers on the railway."""
+    from junqi_b200 import workloads
+    n, seed = 96, 21 + int(late)
+    pool = tables.build_setup_pool(64, seed=seed)
+    env = JunqiEnvB200(n, pool=pool, with_obs=False, rules=N.RULES_GAMESTATE)
+    if late:
+        workloads.late_game_starts(env, seed)
+    else:
+        env.reset(seed=seed)
+    for t in range(1, 121):
+        if t % 10 == 1:
+            orc = O.OracleBatch(n, env.show_mode, rules=N.RULES_GAMESTATE)
+            O.load_state(orc, env.state(), init_beliefs=False)
+            for seats in (None, np.full(n, t % 4, np.int8)):
+                got = env.legal_slots(None if seats is None else torch.from_numpy(seats)).cpu().numpy().astype(bool)
+                exp, _ = orc.slot_mask(seats)
+                if not np.array_equal(got, exp):
+                    e, p, s = np.argwhere(got != exp)[0]
+                    raise AssertionError(f"ply {t}: slot mask differs at env {e} pid {p} slot {s}")
+        env.ply(env.sample_uniform(seed, t), seed=seed, ply=t)
