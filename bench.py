@@ -47,6 +47,7 @@ CONFIGS = {
 }
 
 OBS_WRITE = 317 * 289 * 4 + 28 * 4  # bytes written per (env, seat) observation
+EVENT_EVERY = 8  # timed plies between plies that carry per-kernel CUDA events
 
 # jq_batch.rules: 1 = GameState.step (state.py; Q12 "no legal move -> seat
 # dies" on every ply, as the single-env JunqiEnv and the reference GPU kernel
@@ -283,14 +284,13 @@ def main() -> None:
         env.ply(acts, seed=seed, ply=t)
         if ev is not None:
             ev[3].record(stream)
-        return env.out["valid"]
 
-    applied = torch.zeros(n, dtype=torch.int32, device=env.device)
     for t in range(1, args.warmup + 1):  # same ops as the timed loop, so every kernel is loaded
-        applied += one_ply(t)
-    env.stats.zero_()
-    applied.zero_()
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+        one_ply(t, [torch.cuda.Event(enable_timing=True) for _ in range(4)] if t % EVENT_EVERY == 0 else None)
+    env.stats.zero_()  # jq_ply counts plies applied and episode statistics on the device
+    # Per-kernel CUDA events on every EVENT_EVERY-th timed ply: an event between
+    # two kernels keeps the next launch from overlapping the previous one's tail.
+    evs = {k: [torch.cuda.Event(enable_timing=True) for _ in range(4)] for k in range(0, args.steps, EVENT_EVERY)}
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     clock_rows, stop = [], threading.Event()
     th = threading.Thread(target=sample_clocks, args=(local, stop, clock_rows), daemon=True)
@@ -303,7 +303,7 @@ def main() -> None:
     start.record(stream)
     for k in range(args.steps):
         t = args.warmup + 1 + k
-        applied += one_ply(t, evs[k])
+        one_ply(t, evs.get(k))
     if world > 1:
         sharding.reduce_episode_stats(env.stats)  # one collective per rollout: episode statistics
     end.record(stream)
@@ -314,11 +314,11 @@ def main() -> None:
     stop.set()
     th.join(timeout=10)
     ms_total = start.elapsed_time(end)
-    obs_ms = [e[0].elapsed_time(e[1]) for e in evs]
-    ply_ms = [e[2].elapsed_time(e[3]) for e in evs]
-    plies_local = int(applied.sum(dtype=torch.int64).item())
+    obs_ms = [e[0].elapsed_time(e[1]) for e in evs.values()]
+    ply_ms = [e[2].elapsed_time(e[3]) for e in evs.values()]
+    stats = env.stats.cpu().numpy().tolist()  # summed over ranks inside the timed region
     ms_max = sharding.max_over_ranks(ms_total, env.device)
-    plies_all = sharding.sum_over_ranks(plies_local, env.device)
+    plies_all = int(stats[5])
     value = plies_all / (ms_max / 1e3)
 
     k_avg = float(env.counts.sum(dtype=torch.int64).item()) / n  # legal actions per env, last ply
@@ -327,8 +327,6 @@ def main() -> None:
     e2e = None
     if not args.no_e2e:
         e2e = run_e2e(env, args, seed, stream)
-    stats = env.stats.cpu().numpy().tolist()
-
     if rank == 0:
         peak, peak_kind = peak_hbm()
         units = n * seats
@@ -354,6 +352,8 @@ def main() -> None:
             "pipeline": pipeline_roofline(value / world, seats, k_avg, peak),
             "clocks": summarize_clocks(clock_rows),
             "gpu_launches": 3 * args.steps,  # obs_kernel + sample kernel + rules_kernel per ply
+            "kernel_timing": f"CUDA events around each kernel on every {EVENT_EVERY}th timed ply "
+                             f"({len(obs_ms)} plies)",
             "episode_stats": {"wins_team0": stats[0], "wins_team1": stats[1], "draws": stats[2],
                               "episodes": stats[3], "sum_len": stats[4]},
             "wall_s": t_wall,

@@ -16,7 +16,7 @@
 #include <stddef.h>
 #include <stdint.h>
 
-#define JQ_ABI_VERSION 2
+#define JQ_ABI_VERSION 3
 
 #define JQ_NUM_PIECES 120
 #define JQ_NUM_CELLS 289
@@ -196,8 +196,10 @@ int jq_step_canonical(const jq_batch *b, const int32_t *d_compact_actions,
 /* Fused ply: jq_step, then auto-reset of the envs it terminated (pool
  * index from (seed, ply, env)), then legal generation for the new turn
  * (see jq_legal).  d_world_actions may be NULL to skip the step.  When
- * d_stats is not NULL, each termination adds to d_stats[5] = {wins team 0,
- * wins team 1, draws, episodes, sum of episode lengths in plies}. */
+ * d_stats is not NULL it accumulates int64[6] = {wins team 0, wins team 1,
+ * draws, episodes, sum of episode lengths in plies, plies applied}: the
+ * first five are the reference's per-rollout episode statistics, added at
+ * each termination; the sixth counts steps with valid = 1. */
 int jq_ply(const jq_batch *b, const int32_t *d_world_actions, int32_t show_mode,
            const jq_step_out *out, int32_t autoreset, uint64_t seed, uint64_t ply,
            int32_t *d_counts, int32_t *d_ids, int32_t cap, uint8_t *d_mask,

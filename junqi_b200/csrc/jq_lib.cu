@@ -26,6 +26,7 @@ enum : int { DO_STEP = 1, DO_RESET = 2, DO_LEGAL = 4, RESET_ALL = 8, DO_BELIEF_I
 struct RuleSmem {
     Topo topo;
     WEnv w[RULE_WARPS];
+    int applied;  // plies applied by this CTA (statistics)
 };
 
 struct RuleArgs {
@@ -60,6 +61,7 @@ __global__ void __launch_bounds__(RULE_THREADS, 4) rules_kernel(RuleArgs a) {
         for (int k = (int)(sizeof(Topo) / 16) * 16 + threadIdx.x; k < (int)sizeof(Topo); k += RULE_THREADS)
             d8[k] = s8[k];
     }
+    if (threadIdx.x == 0) S.applied = 0;
     __syncthreads();
     const Topo &T = S.topo;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -74,7 +76,10 @@ __global__ void __launch_bounds__(RULE_THREADS, 4) rules_kernel(RuleArgs a) {
             if (lane == 0) b.hist_count[e] = 0;
             __syncwarp();
         }
-        if (a.flags & DO_STEP) warp_step(b, T, w, e, lane, a.acts[e], a.mode, a.out, a.stats);
+        if (a.flags & DO_STEP) {
+            const bool applied = warp_step(b, T, w, e, lane, a.acts[e], a.mode, a.out, a.stats);
+            if (applied && lane == 0 && a.stats) atomicAdd_block(&S.applied, 1);
+        }
         if (a.flags & DO_RESET) {
             bool do_it = (a.flags & RESET_ALL) || b.terminated[e];
             if (do_it && a.pool && a.pool_size > 0) {
@@ -93,6 +98,8 @@ __global__ void __launch_bounds__(RULE_THREADS, 4) rules_kernel(RuleArgs a) {
         }
         __syncwarp();
     }
+    __syncthreads();
+    if (threadIdx.x == 0 && a.stats && S.applied) atomicAdd((unsigned long long *)&a.stats[5], (unsigned long long)S.applied);
 }
 
 // Zobrist hash of every env rebuilt from scratch (state.py:1761-1815), one

@@ -82,7 +82,7 @@ class JunqiEnvB200:
         self.csr_scratch = torch.zeros(max(1, N.lib().jq_csr_scratch_ints(n)), dtype=torch.int32, device=dev)
         self.actions = torch.full((n,), -1, dtype=torch.int32, device=dev)
         self.compact_actions = torch.full((n,), -1, dtype=torch.int32, device=dev)
-        self.stats = torch.zeros(5, dtype=torch.int64, device=dev)
+        self.stats = torch.zeros(6, dtype=torch.int64, device=dev)  # see sharding.STAT_NAMES
         if with_obs:
             u = n * self.obs_seats
             self.spatial = torch.empty((u, OBS_CHANNELS, 17, 17), dtype=torch.float32, device=dev)

@@ -17,7 +17,9 @@ import torch
 import torch.distributed as dist
 
 RANK_SEED_STRIDE = 10_000
-STAT_NAMES = ("wins_team0", "wins_team1", "draws", "episodes", "sum_len")
+# jq_ply's statistics vector: the reference's per-rollout episode statistics
+# (wins per team, draws, episodes, summed episode length) plus plies applied
+STAT_NAMES = ("wins_team0", "wins_team1", "draws", "episodes", "sum_len", "plies_applied")
 
 
 def _world() -> int:

@@ -156,13 +156,15 @@ def test_episode_stats_count_terminations():
     pool = tables.build_setup_pool(64, seed=9)
     env = JunqiEnvB200(64, pool=pool, with_obs=False)
     env.reset(seed=3)
-    ends = 0
+    ends = applied = 0
     for t in range(1, 1501):
         env.ply(env.sample_uniform(3, t), seed=3, ply=t)
         ends += int(env.out["terminated"].sum().item())
+        applied += int(env.out["valid"].sum().item())
     s = env.stats.cpu().numpy()
     assert s[3] == ends
     assert s[0] + s[1] + s[2] == s[3]
+    assert s[5] == applied
 
 
 def test_step_canonical_equals_world_step():

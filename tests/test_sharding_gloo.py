@@ -28,8 +28,9 @@ def _free_port() -> int:
 
 
 def shard_rollout(rank: int) -> tuple[np.ndarray, int]:
-    """Episode stats (wins0, wins1, draws, episodes, sum_len) and applied plies
-    of rank's slice: GameState rules, uniform policy, auto-reset."""
+    """Statistics vector (wins0, wins1, draws, episodes, sum_len, plies
+    applied) and applied plies of rank's slice: GameState rules, uniform
+    policy, auto-reset."""
     from oracle import oracle as O
     seed = sharding.rank_seed(SEED, rank)
     pool = tables.build_setup_pool(32, seed=seed)
@@ -37,7 +38,7 @@ def shard_rollout(rank: int) -> tuple[np.ndarray, int]:
     rng = np.random.default_rng(seed)
     for e in range(ENVS):
         b.reset_env(e, pool[e % len(pool)])
-    stats = np.zeros(5, np.int64)
+    stats = np.zeros(6, np.int64)
     applied = 0
     for _ in range(PLIES):
         off, val = b.legal()
@@ -55,6 +56,7 @@ def shard_rollout(rank: int) -> tuple[np.ndarray, int]:
             stats[3] += 1
             stats[4] += int(b["move_counter"][e])
             b.reset_env(int(e), pool[int(rng.integers(len(pool)))])
+    stats[5] = applied
     return stats, applied
 
 
@@ -80,12 +82,12 @@ def test_rank_seed_and_env_slice():
     with pytest.raises(ValueError):
         sharding.env_slice(10, 4, 4)
     with pytest.raises(ValueError):
-        sharding.reduce_episode_stats(torch.zeros(5, dtype=torch.int32))
+        sharding.reduce_episode_stats(torch.zeros(6, dtype=torch.int32))
 
 
 def test_single_process_reductions_are_identity():
-    t = torch.tensor([1, 2, 3, 4, 5], dtype=torch.int64)
-    assert sharding.reduce_episode_stats(t) is t and t.tolist() == [1, 2, 3, 4, 5]
+    t = torch.tensor([1, 2, 3, 4, 5, 6], dtype=torch.int64)
+    assert sharding.reduce_episode_stats(t) is t and t.tolist() == [1, 2, 3, 4, 5, 6]
     assert sharding.max_over_ranks(2.5) == 2.5 and sharding.sum_over_ranks(7) == 7
     assert sharding.stats_dict(t)["episodes"] == 4
 
@@ -101,7 +103,7 @@ def test_two_gloo_ranks_reduce_episode_stats_of_independent_slices():
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    expect_stats = np.zeros(5, np.int64)
+    expect_stats = np.zeros(6, np.int64)
     expect_tot = 0
     for r in range(2):
         s, a = shard_rollout(r)
