@@ -52,6 +52,7 @@ struct StepCtx {
     int skip, ev, A, D, sf, df, acting, A_type, A_seat, D_type, D_seat;
     int mc, mslc, new_mc, new_mslc, fcap, fr_src, fr_dst, other_pid, term, win, draw;
     int new_turn, need_surrender, do_q12, combat, full_advance;
+    int cm;  // combat-memory update after the scalar part: 0 none, 1 EAT, 2 KILLED
     int died_pre[4];
 };
 
@@ -65,25 +66,81 @@ struct __align__(16) WEnv {
     int8_t seat[NP];
     uint8_t alive[NP];
     uint8_t sdead[4];
+    // the env's scalars as loaded before the ply (read by the step)
+    int64_t s_zob;
+    int32_t s_mc, s_mslc, s_hc;
+    int8_t s_turn, s_term, s_win, s_draw;
+    uint8_t sflag[4];  // seat_flag, kept in step with the global copy during the ply
 };
 
 __device__ __forceinline__ size_t PI(int e, int p) { return (size_t)e * NP + p; }
 __device__ __forceinline__ size_t OI(int e, int o, int p) { return ((size_t)e * 4 + o) * NP + p; }
 
+// Every load is issued before any shared-memory store, so the warp waits
+// for global memory once.
 __device__ void warp_load(const jq_batch &b, const Topo &T, WEnv &w, int e, int lane) {
-    for (int f = lane; f < NC; f += 32) {
-        int p = b.cell_pid[(size_t)e * NC + f];
-        w.cell[f] = (int16_t)((p >= 0 && p < NP) ? p : -1);
+    constexpr int CI = (NC + 31) / 32, PIT = (NP + 31) / 32;
+    int cp[CI];
+#pragma unroll
+    for (int i = 0; i < CI; ++i) {
+        const int f = lane + 32 * i;
+        cp[i] = f < NC ? b.cell_pid[(size_t)e * NC + f] : -1;
     }
-    for (int p = lane; p < NP; p += 32) {
-        size_t q = PI(e, p);
-        w.alive[p] = b.alive[q];
-        w.type[p] = b.piece_type[q];
-        w.seat[p] = b.piece_seat[q];
-        int x = b.pos_x[q], y = b.pos_y[q];
-        w.posc[p] = (int16_t)((x >= 0 && x < 17 && y >= 0 && y < 17) ? T.f2c[y * 17 + x] : -1);
+    int al[PIT], ty[PIT], se[PIT], px[PIT], py[PIT];
+#pragma unroll
+    for (int i = 0; i < PIT; ++i) {
+        const int p = lane + 32 * i;
+        if (p < NP) {
+            const size_t q = PI(e, p);
+            al[i] = b.alive[q];
+            ty[i] = b.piece_type[q];
+            se[i] = b.piece_seat[q];
+            px[i] = b.pos_x[q];
+            py[i] = b.pos_y[q];
+        }
     }
-    if (lane < 4) w.sdead[lane] = b.seat_dead[(size_t)e * 4 + lane];
+    int64_t sc = 0;
+    switch (lane) {
+    case 0: sc = b.terminated[e]; break;
+    case 1: sc = b.turn[e]; break;
+    case 2: sc = b.move_counter[e]; break;
+    case 3: sc = b.mslc[e]; break;
+    case 4: sc = b.zobrist[e]; break;
+    case 5: sc = b.hist_count[e]; break;
+    case 6: sc = b.winner[e]; break;
+    case 7: sc = b.draw[e]; break;
+    case 8: case 9: case 10: case 11: sc = b.seat_dead[(size_t)e * 4 + lane - 8]; break;
+    case 12: case 13: case 14: case 15: sc = b.seat_flag[(size_t)e * 4 + lane - 12]; break;
+    default: break;
+    }
+#pragma unroll
+    for (int i = 0; i < CI; ++i) {
+        const int f = lane + 32 * i;
+        if (f < NC) w.cell[f] = (int16_t)((cp[i] >= 0 && cp[i] < NP) ? cp[i] : -1);
+    }
+#pragma unroll
+    for (int i = 0; i < PIT; ++i) {
+        const int p = lane + 32 * i;
+        if (p < NP) {
+            w.alive[p] = (uint8_t)al[i];
+            w.type[p] = (int8_t)ty[i];
+            w.seat[p] = (int8_t)se[i];
+            w.posc[p] = (int16_t)((px[i] >= 0 && px[i] < 17 && py[i] >= 0 && py[i] < 17) ? T.f2c[py[i] * 17 + px[i]] : -1);
+        }
+    }
+    switch (lane) {
+    case 0: w.s_term = (int8_t)sc; break;
+    case 1: w.s_turn = (int8_t)sc; break;
+    case 2: w.s_mc = (int32_t)sc; break;
+    case 3: w.s_mslc = (int32_t)sc; break;
+    case 4: w.s_zob = sc; break;
+    case 5: w.s_hc = (int32_t)sc; break;
+    case 6: w.s_win = (int8_t)sc; break;
+    case 7: w.s_draw = (int8_t)sc; break;
+    case 8: case 9: case 10: case 11: w.sdead[lane - 8] = (uint8_t)sc; break;
+    case 12: case 13: case 14: case 15: w.sflag[lane - 12] = (uint8_t)sc; break;
+    default: break;
+    }
     __syncwarp();
 }
 
@@ -407,88 +464,82 @@ __device__ __forceinline__ int next_floor(int t) {
     return r > 9 ? 9 : r;
 }
 
-__device__ void cm_apply(const jq_batch &b, int e, bool eat, int A, int D, int A_seat, int D_seat, int A_type,
-                         int D_type, int step) {
-    int K = eat ? A : D, V = eat ? D : A, V_seat = eat ? D_seat : A_seat, V_type = eat ? D_type : A_type;
-    int v_idx = tracked_idx(V_type);
-    if (!eat)
-        for (int o = 0; o < 4; ++o)
-            if (b.cm_is_gongb[OI(e, o, V)] || (A_type == GONGB && o == V_seat)) b.cm_atk_gongb[OI(e, o, K)] = 1;
-    for (int o = 0; o < 4; ++o) {
-        size_t k = OI(e, o, K), v = OI(e, o, V);
+// The update touches three disjoint sets of rows, so the warp splits it:
+// lanes 0..3 take observer o = lane (the attacked-by-known-engineer flag,
+// chain propagation, then the direct update, all on K's row of o), and
+// lanes 0..29 take the reverse projection onto pid o * 30 + lane of every
+// observer o (reads V's rows, writes eaten-by rows).  The per-observer order
+// of the scalar statement is kept; the three parts commute (OR / max
+// updates of different rows).
+__device__ void warp_cm_apply(const jq_batch &b, int e, int lane, bool eat, int A, int D, int A_seat, int D_seat,
+                              int A_type, int D_type, int step) {
+    const int K = eat ? A : D, V = eat ? D : A, V_seat = eat ? D_seat : A_seat, V_type = eat ? D_type : A_type;
+    const int v_idx = tracked_idx(V_type);
+    if (lane < 4) {
+        const int o = lane;
+        const size_t k = OI(e, o, K), v = OI(e, o, V);
+        if (!eat && (b.cm_is_gongb[v] || (A_type == GONGB && o == V_seat))) b.cm_atk_gongb[k] = 1;
         uint64_t lo = b.cm_chain_lo[k] | b.cm_direct_lo[v] | b.cm_chain_lo[v];
         uint64_t hi = b.cm_chain_hi[k] | b.cm_direct_hi[v] | b.cm_chain_hi[v];
         set_pid_bit(lo, hi, V);
         b.cm_chain_lo[k] = lo;
         b.cm_chain_hi[k] = hi;
-        b.cm_chain_type[k] = (uint16_t)(b.cm_chain_type[k] | b.cm_direct_type[v] | b.cm_chain_type[v]);
-        b.cm_last_chain_step[k] = (int16_t)step;
-        int vf = b.cm_rank_floor[v], prop = vf + 1 < 9 ? vf + 1 : 9;
+        uint16_t ctype = (uint16_t)(b.cm_chain_type[k] | b.cm_direct_type[v] | b.cm_chain_type[v]);
+        int floor_k = b.cm_rank_floor[k];
+        bool floor_up = false, not_g = false;
+        const int vf = b.cm_rank_floor[v], prop = vf + 1 < 9 ? vf + 1 : 9;
         if (vf > 0) {
-            if (prop > b.cm_rank_floor[k]) {
-                b.cm_rank_floor[k] = (int8_t)prop;
-                b.cm_rank_floor_step[k] = (int16_t)step;
-            }
-            b.cm_not_gongb[k] = 1;
+            if (prop > floor_k) { floor_k = prop; floor_up = true; }
+            not_g = true;
         }
-    }
-    // reverse projection onto observer-own pids (reads V's rows, untouched above)
-    for (int o = 0; o < 4; ++o) {
-        size_t v = OI(e, o, V);
-        uint64_t mlo = 0, mhi = 0;
-        for (int s = 0; s < 30; ++s) set_pid_bit(mlo, mhi, o * 30 + s);
-        uint64_t lo = (b.cm_direct_lo[v] | b.cm_chain_lo[v]) & mlo;
-        uint64_t hi = (b.cm_direct_hi[v] | b.cm_chain_hi[v]) & mhi;
-        if (V_seat == o) set_pid_bit(lo, hi, V);
-        while (lo) {
-            int t = __ffsll((long long)lo) - 1;
-            lo &= lo - 1;
-            size_t tt = OI(e, o, t);
-            uint64_t a = b.cm_eaten_lo[tt], c = b.cm_eaten_hi[tt];
-            set_pid_bit(a, c, K);
-            b.cm_eaten_lo[tt] = a;
-            b.cm_eaten_hi[tt] = c;
-        }
-        while (hi) {
-            int t = 64 + __ffsll((long long)hi) - 1;
-            hi &= hi - 1;
-            if (t >= NP) continue;
-            size_t tt = OI(e, o, t);
-            uint64_t a = b.cm_eaten_lo[tt], c = b.cm_eaten_hi[tt];
-            set_pid_bit(a, c, K);
-            b.cm_eaten_lo[tt] = a;
-            b.cm_eaten_hi[tt] = c;
-        }
-    }
-    for (int o = 0; o < 4; ++o) {
-        size_t k = OI(e, o, K);
         if (V_seat != o) {
-            int c = b.cm_direct_other[k] + 1;
+            const int c = b.cm_direct_other[k] + 1;
             b.cm_direct_other[k] = (int16_t)(c < 32767 ? c : 32767);
-            b.cm_last_direct_step[k] = (int16_t)step;
-            continue;
+        } else {
+            uint64_t dlo = b.cm_direct_lo[k], dhi = b.cm_direct_hi[k];
+            set_pid_bit(dlo, dhi, V);
+            b.cm_direct_lo[k] = dlo;
+            b.cm_direct_hi[k] = dhi;
+            if (v_idx >= 0) {
+                b.cm_direct_type[k] = (uint16_t)(b.cm_direct_type[k] | (1u << v_idx));
+                ctype = (uint16_t)(ctype | (1u << v_idx));
+            }
+            if (eat) {
+                if (V_type == DILEI) b.cm_is_gongb[k] = 1;
+                else not_g = true;
+            }
+            if (is_ranked(V_type)) {  // KILLED defender lift and EAT-direct lift use the same rule
+                const int pr = next_floor(V_type);
+                if (pr > floor_k) { floor_k = pr; floor_up = true; }
+            }
         }
-        uint64_t lo = b.cm_direct_lo[k], hi = b.cm_direct_hi[k];
-        set_pid_bit(lo, hi, V);
-        b.cm_direct_lo[k] = lo;
-        b.cm_direct_hi[k] = hi;
-        if (v_idx >= 0) {
-            b.cm_direct_type[k] = (uint16_t)(b.cm_direct_type[k] | (1u << v_idx));
-            b.cm_chain_type[k] = (uint16_t)(b.cm_chain_type[k] | (1u << v_idx));
-        }
+        b.cm_chain_type[k] = ctype;
+        b.cm_last_chain_step[k] = (int16_t)step;
         b.cm_last_direct_step[k] = (int16_t)step;
-        if (eat) {
-            if (V_type == DILEI) b.cm_is_gongb[k] = 1;
-            else b.cm_not_gongb[k] = 1;
+        if (floor_up) {
+            b.cm_rank_floor[k] = (int8_t)floor_k;
+            b.cm_rank_floor_step[k] = (int16_t)step;
         }
-        if (is_ranked(V_type)) {  // KILLED defender lift and EAT-direct lift use the same rule
-            int pr = next_floor(V_type);
-            if (pr > b.cm_rank_floor[k]) {
-                b.cm_rank_floor[k] = (int8_t)pr;
-                b.cm_rank_floor_step[k] = (int16_t)step;
+        if (not_g) b.cm_not_gongb[k] = 1;
+    }
+    if (lane < 30) {
+        // reverse projection: observer-own pid o * 30 + lane gains K in its eaten-by set
+        // when V's direct or chain set (of observer o) holds it, or it is V itself
+        for (int o = 0; o < 4; ++o) {
+            const size_t v = OI(e, o, V);
+            const int t = o * 30 + lane;
+            const uint64_t lo = b.cm_direct_lo[v] | b.cm_chain_lo[v], hi = b.cm_direct_hi[v] | b.cm_chain_hi[v];
+            const bool on = (t < 64 ? (lo >> t) & 1ull : (hi >> (t - 64)) & 1ull) || (V_seat == o && t == V);
+            if (on) {
+                const size_t tt = OI(e, o, t);
+                uint64_t a = b.cm_eaten_lo[tt], c = b.cm_eaten_hi[tt];
+                set_pid_bit(a, c, K);
+                b.cm_eaten_lo[tt] = a;
+                b.cm_eaten_hi[tt] = c;
             }
         }
     }
+    __syncwarp();
 }
 
 // ---------------------------------------------------------------------------
@@ -504,9 +555,13 @@ __device__ __forceinline__ uint8_t initial_code(const Topo &T, const WEnv &w, in
     if (!w.alive[p]) return BC_NONE;
     int s = w.seat[p];
     if (sees_truth(o, s, mode)) return (uint8_t)(tracked_idx(w.type[p]) + 1);
-    if (s >= 0 && s < 4)
+    if (s >= 0 && s < 4) {
+        // a piece on its own setup cell (every piece right after a reset) has
+        // that slot; otherwise search the seat's slots for its cell
+        if (T.slot_cell[s][p % 30] == w.posc[p]) return (uint8_t)(BC_PRIOR0 + p % 30);
         for (int i = 0; i < 30; ++i)
             if (T.slot_cell[s][i] == w.posc[p]) return (uint8_t)(BC_PRIOR0 + i);
+    }
     return BC_UNIFORM;
 }
 
@@ -760,12 +815,12 @@ __device__ bool warp_step(const jq_batch &b, const Topo &T, WEnv &w, int e, int 
     int64_t zob = 0;
     if (lane == 0) {
         x.skip = 1;
-        int term0 = b.terminated[e];
+        int term0 = w.s_term;
         out.valid[e] = 0;
         if (out.event) out.event[e] = 0;
         if (out.terminated) out.terminated[e] = (uint8_t)term0;
-        if (out.winner) out.winner[e] = b.winner[e];
-        if (out.draw) out.draw[e] = b.draw[e];
+        if (out.winner) out.winner[e] = w.s_win;
+        if (out.draw) out.draw[e] = (uint8_t)w.s_draw;
         if (out.flag_captured) out.flag_captured[e] = 0;
         if (out.reward) out.reward[e] = 0.f;
         if (!term0 && act >= 0 && act < NC * NC) {
@@ -784,15 +839,16 @@ __device__ bool warp_step(const jq_batch &b, const Topo &T, WEnv &w, int e, int 
     if (x.skip) return false;
     if (lane == 0) {
         const int sf = x.sf, df = x.df, A = x.A, D = x.D;
-        x.acting = b.turn[e];
-        x.mc = b.move_counter[e];
-        x.mslc = b.mslc[e];
+        x.acting = w.s_turn;
+        x.mc = w.s_mc;
+        x.mslc = w.s_mslc;
         x.new_mc = x.mc + 1;
         x.combat = D >= 0;
         for (int s = 0; s < 4; ++s) x.died_pre[s] = w.sdead[s];
         x.other_pid = -1;
         x.fcap = x.fr_src = x.fr_dst = 0;
         x.need_surrender = 0;
+        x.cm = 0;
         if (D >= 0 && x.D_seat >= 0 && x.D_seat < 4) {
             int s0 = T.c2f[T.slot_cell[x.D_seat][26]], s1 = T.c2f[T.slot_cell[x.D_seat][28]];
             if (df == s0) x.other_pid = w.cell[s1];
@@ -803,7 +859,7 @@ __device__ bool warp_step(const jq_batch &b, const Topo &T, WEnv &w, int e, int 
             if ((D >= 0 || adx + ady > 1) && move_requires_gongb(T, w, sf, df))
                 for (int o = 0; o < 4; ++o) b.cm_is_gongb[OI(e, o, A)] = 1;
         }
-        zob = b.zobrist[e] ^ c_zturn[x.acting & 3] ^ g_zmc[x.mc & 0xFFF] ^ g_zmslc[x.mslc & 0x1FF];
+        zob = w.s_zob ^ c_zturn[x.acting & 3] ^ g_zmc[x.mc & 0xFFF] ^ g_zmslc[x.mslc & 0x1FF];
         if (D < 0) {
             zob ^= zpiece(A, x.A_type, sf) ^ zpiece(A, x.A_type, df);
             move_piece(b, T, w, e, A, sf, df);
@@ -813,11 +869,13 @@ __device__ bool warp_step(const jq_batch &b, const Topo &T, WEnv &w, int e, int 
             int ds = x.new_mc;
             x.fr_src = x.A_type == SILING && (x.ev == EV_KILLED || x.ev == EV_BOMB);
             x.fr_dst = x.D_type == SILING && (x.ev == EV_EAT || x.ev == EV_BOMB);
-            if (x.fr_src && x.A_seat >= 0 && x.A_seat < 4 && !b.seat_flag[(size_t)e * 4 + x.A_seat]) {
+            if (x.fr_src && x.A_seat >= 0 && x.A_seat < 4 && !w.sflag[x.A_seat]) {
+                w.sflag[x.A_seat] = 1;
                 b.seat_flag[(size_t)e * 4 + x.A_seat] = 1;
                 zob ^= c_zsflag[x.A_seat];
             }
-            if (x.fr_dst && x.D_seat >= 0 && x.D_seat < 4 && !b.seat_flag[(size_t)e * 4 + x.D_seat]) {
+            if (x.fr_dst && x.D_seat >= 0 && x.D_seat < 4 && !w.sflag[x.D_seat]) {
+                w.sflag[x.D_seat] = 1;
                 b.seat_flag[(size_t)e * 4 + x.D_seat] = 1;
                 zob ^= c_zsflag[x.D_seat];
             }
@@ -828,13 +886,13 @@ __device__ bool warp_step(const jq_batch &b, const Topo &T, WEnv &w, int e, int 
                 zob ^= zpiece(A, x.A_type, sf) ^ zpiece(A, x.A_type, df);
                 move_piece(b, T, w, e, A, sf, df);
                 b.active_eat[PI(e, A)]++;
-                cm_apply(b, e, true, A, D, x.A_seat, x.D_seat, x.A_type, x.D_type, ds);
+                x.cm = 1;
             } else if (x.ev == EV_KILLED) {
                 int dr = (x.D_type == DILEI || x.D_type == ZHADAN) ? DR_MINE : DR_KBE;
                 zob ^= zpiece(A, x.A_type, sf);
                 kill_piece(b, T, w, e, A, sf, dr, ds, df);
                 b.passive_surv[PI(e, D)]++;
-                cm_apply(b, e, false, A, D, x.A_seat, x.D_seat, x.A_type, x.D_type, ds);
+                x.cm = 2;
             } else {
                 zob ^= zpiece(A, x.A_type, sf) ^ zpiece(D, x.D_type, df);
                 kill_piece(b, T, w, e, A, sf, DR_MUTUAL, ds, df);
@@ -842,7 +900,8 @@ __device__ bool warp_step(const jq_batch &b, const Topo &T, WEnv &w, int e, int 
             }
             x.new_mslc = 0;
             if (x.fcap && x.D_seat >= 0 && x.D_seat < 4 && !w.sdead[x.D_seat]) {
-                if (!b.seat_flag[(size_t)e * 4 + x.D_seat]) {
+                if (!w.sflag[x.D_seat]) {
+                    w.sflag[x.D_seat] = 1;
                     b.seat_flag[(size_t)e * 4 + x.D_seat] = 1;
                     zob ^= c_zsflag[x.D_seat];
                 }
@@ -851,6 +910,7 @@ __device__ bool warp_step(const jq_batch &b, const Topo &T, WEnv &w, int e, int 
         }
     }
     __syncwarp();
+    if (x.cm) warp_cm_apply(b, e, lane, x.cm == 1, x.A, x.D, x.A_seat, x.D_seat, x.A_type, x.D_type, x.new_mc);
     if (x.need_surrender) {
         int64_t d = warp_surrender(b, T, w, e, lane, x.D_seat, x.new_mc);
         if (lane == 0) zob ^= d;
@@ -920,7 +980,7 @@ __device__ bool warp_step(const jq_batch &b, const Topo &T, WEnv &w, int e, int 
         if (out.flag_captured) out.flag_captured[e] = (uint8_t)x.fcap;
         if (out.reward)
             out.reward[e] = (x.term && !x.draw && x.win >= 0) ? (((x.acting & 1) == x.win) ? 1.f : -1.f) : 0.f;
-        int hc = b.hist_count[e];
+        int hc = w.s_hc;
         b.hist_src[(size_t)e * HIST + (hc & (HIST - 1))] = (int16_t)x.sf;
         b.hist_dst[(size_t)e * HIST + (hc & (HIST - 1))] = (int16_t)x.df;
         b.hist_count[e] = hc + 1;
