@@ -12,95 +12,12 @@
 #include <mutex>
 
 #include "jq_obs.cuh"
+#include "jq_ply.cuh"
 #include "jq_rules.cuh"
 #include "jq_slots.cuh"
 #include "jq_topo_build.h"
 
 namespace jq {
-
-constexpr int RULE_WARPS = 8;
-constexpr int RULE_THREADS = RULE_WARPS * 32;
-
-enum : int { DO_STEP = 1, DO_RESET = 2, DO_LEGAL = 4, RESET_ALL = 8, DO_BELIEF_INIT = 16 };
-
-struct RuleSmem {
-    Topo topo;
-    WEnv w[RULE_WARPS];
-    int applied;  // plies applied by this CTA (statistics)
-};
-
-struct RuleArgs {
-    jq_batch b;
-    const int32_t *acts;
-    int mode;
-    jq_step_out out;
-    uint64_t seed, ply;
-    const int8_t *pool;
-    int pool_size;
-    int32_t *counts, *ids;
-    int cap;
-    uint8_t *mask;
-    int64_t *stats;
-    const int8_t *seats;
-    int flags;
-};
-
-__device__ __forceinline__ int pool_index(uint64_t seed, uint64_t ply, int e, int P) {
-    return (int)(hash3(seed, ply, (uint64_t)e) % (uint64_t)P);
-}
-
-__global__ void __launch_bounds__(RULE_THREADS, 4) rules_kernel(RuleArgs a) {
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    RuleSmem &S = *reinterpret_cast<RuleSmem *>(smem_raw);
-    {
-        const uint4 *src = reinterpret_cast<const uint4 *>(&g_topo);
-        uint4 *dst = reinterpret_cast<uint4 *>(&S.topo);
-        for (int k = threadIdx.x; k < (int)(sizeof(Topo) / 16); k += RULE_THREADS) dst[k] = src[k];
-        const unsigned char *s8 = reinterpret_cast<const unsigned char *>(&g_topo);
-        unsigned char *d8 = reinterpret_cast<unsigned char *>(&S.topo);
-        for (int k = (int)(sizeof(Topo) / 16) * 16 + threadIdx.x; k < (int)sizeof(Topo); k += RULE_THREADS)
-            d8[k] = s8[k];
-    }
-    if (threadIdx.x == 0) S.applied = 0;
-    __syncthreads();
-    const Topo &T = S.topo;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    WEnv &w = S.w[warp];
-    const jq_batch &b = a.b;
-    for (int e = blockIdx.x * RULE_WARPS + warp; e < b.n; e += gridDim.x * RULE_WARPS) {
-        warp_load(b, T, w, e, lane);
-        if (a.flags & DO_BELIEF_INIT) {
-            warp_belief_init(b, T, w, e, lane, a.mode);
-            b.hist_src[(size_t)e * HIST + lane] = -1;
-            b.hist_dst[(size_t)e * HIST + lane] = -1;
-            if (lane == 0) b.hist_count[e] = 0;
-            __syncwarp();
-        }
-        if (a.flags & DO_STEP) {
-            const bool applied = warp_step(b, T, w, e, lane, a.acts[e], a.mode, a.out, a.stats);
-            if (applied && lane == 0 && a.stats) atomicAdd_block(&S.applied, 1);
-        }
-        if (a.flags & DO_RESET) {
-            bool do_it = (a.flags & RESET_ALL) || b.terminated[e];
-            if (do_it && a.pool && a.pool_size > 0) {
-                const int8_t *lu = a.pool + (size_t)pool_index(a.seed, a.ply, e, a.pool_size) * NP;
-                warp_reset(b, T, w, e, lane, lu, a.mode);
-            }
-        }
-        __syncwarp();
-        if (a.flags & DO_LEGAL) {
-            int seat = a.seats ? a.seats[e] : b.turn[e];
-            bool skip = seat < 0 || seat > 3 || b.terminated[e] || w.sdead[seat & 3];
-            seat &= 3;
-            int cnt = warp_legal(T, w, lane, seat, skip, a.ids ? a.ids + (size_t)e * a.cap : nullptr, a.cap,
-                                 a.mask ? a.mask + (size_t)e * MASK_BYTES : nullptr);
-            if (lane == 0 && a.counts) a.counts[e] = cnt;
-        }
-        __syncwarp();
-    }
-    __syncthreads();
-    if (threadIdx.x == 0 && a.stats && S.applied) atomicAdd((unsigned long long *)&a.stats[5], (unsigned long long)S.applied);
-}
 
 // Zobrist hash of every env rebuilt from scratch (state.py:1761-1815), one
 // warp per env.

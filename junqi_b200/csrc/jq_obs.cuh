@@ -311,7 +311,7 @@ __device__ __forceinline__ int unit_observer(const jq_batch &b, const int8_t *ob
 }
 
 __device__ void stage_unit(const jq_batch &b, int seats, int mode, float *global, ObsSmem &S, UnitBuf &B, int u,
-                           int o, int head, int t) {
+                           int o, int head, int t, int bar_stage) {
     const int e = u / seats;
     const int tm = (o + 2) & 3, left = (o + 1) & 3, right = (o + 3) & 3;
     Stager st{B, 4 - head};
@@ -351,7 +351,7 @@ __device__ void stage_unit(const jq_batch &b, int seats, int mode, float *global
         B.u = u;
         B.exc_n = 0;
     }
-    bar_sync(BAR_STAGE, OBS_STAGE_THREADS);
+    bar_sync(bar_stage, OBS_STAGE_THREADS);
     // pieces, then history / constants / statics (all bit writes are atomic)
     if (t < NP) stage_piece(b, e, o, mode, S, st, t);
     if (t < HIST) {  // move history (observation.py:1207-1231)
@@ -395,8 +395,9 @@ __device__ void stage_unit(const jq_batch &b, int seats, int mode, float *global
     }
 }
 
-// Streaming warps: write unit B.u.  w = streaming warp 0..7, t = its thread 0..255.
-__device__ void stream_unit(const UnitBuf &B, float *spatial, int w, int lane) {
+// Streaming warps: write unit B.u.  w = streaming warp 0..nwarps-1, t = its thread;
+// bar_stream is a named barrier of the nwarps streaming warps.
+__device__ void stream_unit(const UnitBuf &B, float *spatial, int w, int lane, int nwarps, int bar_stream) {
     const int u = B.u, t = w * 32 + lane;
     float *out = spatial + (size_t)u * OBS_FLOATS;
     const int head = unit_head(spatial, u), qoff = 4 - head;
@@ -409,7 +410,7 @@ __device__ void stream_unit(const UnitBuf &B, float *spatial, int w, int lane) {
         if (j < OBS_FLOATS) out[j] = bit_value(B, j, qoff);
     }
     float4 *out4 = reinterpret_cast<float4 *>(out + head);
-    const int per = (body4 + OBS_STREAM_WARPS - 1) / OBS_STREAM_WARPS;
+    const int per = (body4 + nwarps - 1) / nwarps;
     const int g0 = w * per, g1 = g0 + per < body4 ? g0 + per : body4;
 #pragma unroll 4
     for (int g = g0 + lane; g < g1; g += 32) {
@@ -419,9 +420,9 @@ __device__ void stream_unit(const UnitBuf &B, float *spatial, int w, int lane) {
                               (nib & 8u) ? 1.f : 0.f);
     }
     // pass 2: the exceptions, ordered after pass 1 by the streaming warps' barrier
-    bar_sync(BAR_STREAM, 32 * OBS_STREAM_WARPS);
+    bar_sync(bar_stream, 32 * nwarps);
     const int n = B.exc_n < EXC_MAX ? B.exc_n : EXC_MAX;
-    for (int i = t; i < n; i += 32 * OBS_STREAM_WARPS) out[B.exc_pos[i]] = B.exc_val[i];
+    for (int i = t; i < n; i += 32 * nwarps) out[B.exc_pos[i]] = B.exc_val[i];
 }
 
 // Grid: persistent.  ticket[0] hands out units u = e * seats + k in order;
@@ -454,7 +455,7 @@ __global__ void __launch_bounds__(OBS_THREADS, OBS_MIN_CTAS) obs_kernel(jq_batch
             bar_sync(BAR_FULL0 + bi, OBS_THREADS);  // buffer bi staged
             const UnitBuf &B = S.buf[bi];
             if (B.u < 0) break;
-            stream_unit(B, spatial, warp, lane);
+            stream_unit(B, spatial, warp, lane, OBS_STREAM_WARPS, BAR_STREAM);
             bar_arrive(BAR_EMPTY0 + bi, OBS_THREADS);  // buffer bi free again
         }
     } else {
@@ -483,7 +484,7 @@ __global__ void __launch_bounds__(OBS_THREADS, OBS_MIN_CTAS) obs_kernel(jq_batch
                 un = atomicAdd(&ticket[0], 1);
                 on = un < units ? unit_observer(b, observers, seats, un) : 0;
             }
-            stage_unit(b, seats, mode, global, S, B, u, o, unit_head(spatial, u), t);
+            stage_unit(b, seats, mode, global, S, B, u, o, unit_head(spatial, u), t, BAR_STAGE);
             if (t == 0) { S.ticket = un; S.next_o = on; }
             bar_sync(BAR_STAGE, OBS_STAGE_THREADS);  // unit staged; next ticket published
             u = S.ticket;
