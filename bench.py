@@ -391,6 +391,12 @@ def run_e2e(env, args, seed, stream) -> dict:
     applied, h2d, d2h = 0, 0, 0
     steps = args.e2e_steps
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # The host needs only the step results and the legal CSR to choose the next
+    # actions; they are copied on a side stream as soon as the ply is done,
+    # while the observation kernel (consumed on the device by the policy) keeps
+    # running on the main stream.
+    copy_stream = torch.cuda.Stream(device=env.device)
+    csr_done = torch.cuda.Event()
     torch.cuda.synchronize()
     import torch.distributed as dist
     if dist.is_initialized():
@@ -405,15 +411,20 @@ def run_e2e(env, args, seed, stream) -> dict:
         acts_d.copy_(acts_h, non_blocking=True)
         h2d += n * 4
         env.ply(acts_d, seed=seed, ply=100_000 + t)
-        env.observe()
         off, val = env.csr()
-        for k, h in res_h.items():
-            h.copy_(env.out[k], non_blocking=True)
-            d2h += h.numel() * h.element_size()
-        off_h.copy_(off, non_blocking=True)
-        torch.cuda.synchronize()
+        csr_done.record(stream)
+        env.observe()
+        with torch.cuda.stream(copy_stream):
+            copy_stream.wait_event(csr_done)
+            for k, h in res_h.items():
+                h.copy_(env.out[k], non_blocking=True)
+                d2h += h.numel() * h.element_size()
+            off_h.copy_(off, non_blocking=True)
+        copy_stream.synchronize()
         tot = int(off_h[-1])
-        val_h[:tot].copy_(val[:tot])
+        with torch.cuda.stream(copy_stream):
+            val_h[:tot].copy_(val[:tot], non_blocking=True)
+        copy_stream.synchronize()
         d2h += (n + 1) * 4 + tot * 4
         applied += int(res_h["valid"].numpy().sum())
     end.record(stream)
@@ -423,7 +434,8 @@ def run_e2e(env, args, seed, stream) -> dict:
     applied = sharding.sum_over_ranks(applied, env.device)
     return {"value": applied / (ms / 1e3), "unit": "plies/s", "h2d_bytes_per_step": h2d // steps,
             "d2h_bytes_per_step": d2h // steps, "steps": steps,
-            "api": "JunqiEnvB200.ply/observe/csr with pinned host actions in, MoveResult + CSR out"}
+            "api": "JunqiEnvB200.ply/csr/observe with pinned host actions in, MoveResult + CSR out (side-stream "
+                   "copies overlap the observation kernel)"}
 
 
 if __name__ == "__main__":
