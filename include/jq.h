@@ -205,6 +205,27 @@ int jq_ply(const jq_batch *b, const int32_t *d_world_actions, int32_t show_mode,
            int32_t *d_counts, int32_t *d_ids, int32_t cap, uint8_t *d_mask,
            int64_t *d_stats, void *stream);
 
+/* Compact rollout history (replaces DeviceRolloutHistory, junqi_cuda.h:186-277,
+ * bindings.cpp:728-800).  The caller owns a 16-byte aligned device buffer of
+ * num_steps x N records of jq_history_record_bytes() bytes each; a record
+ * holds what the observation and the legal mask of one seat read: the
+ * board and piece state, that observer's combat-memory row, belief codes and
+ * inventories, and the two opponents' views of its own pieces. */
+int32_t jq_history_record_bytes(void);
+
+/* Record every env of b (observer d_seats[e], NULL: its turn) as step `step`
+ * of the history: record step * N + e. */
+int jq_history_snapshot(const jq_batch *b, const int8_t *d_seats, void *d_history, int64_t step,
+                        int64_t num_steps, void *stream);
+
+/* Restore records d_indices[0 .. scratch->n) (flat step * N + env; out of
+ * range: an empty, terminated env) into the envs of `scratch`, writing each
+ * record's observer to d_observers.  jq_legal(scratch, d_observers, ...) and
+ * jq_observe(scratch, d_observers, 1, ...) then rebuild the recorded seat's
+ * legal actions, canonical mask and observation exactly as they were. */
+int jq_history_restore(const void *d_history, int64_t num_records, const int64_t *d_indices,
+                       const jq_batch *scratch, int8_t *d_observers, void *stream);
+
 /* Legal actions for `d_seats` (NULL: each env's turn), ascending and
  * de-duplicated per env (BatchedGameState.legal_action_ids_batch,
  * batched_state.py:370-409).  Writes d_counts (N) and d_ids (N x cap);

@@ -70,6 +70,9 @@ SIGNATURES = {
     "jq_init_beliefs": (ctypes.c_int, [_PB, _i32, _vp]),
     "jq_rehash": (ctypes.c_int, [_PB, _i32, _vp]),
     "jq_legal_slots": (ctypes.c_int, [_PB, _vp, _vp, _vp]),
+    "jq_history_record_bytes": (_i32, []),
+    "jq_history_snapshot": (ctypes.c_int, [_PB, _vp, _vp, ctypes.c_int64, ctypes.c_int64, _vp]),
+    "jq_history_restore": (ctypes.c_int, [_vp, ctypes.c_int64, _vp, _PB, _vp, _vp]),
     "jq_step": (ctypes.c_int, [_PB, _vp, _i32, _PO, _vp]),
     "jq_step_canonical": (ctypes.c_int, [_PB, _vp, _vp, _i32, _PO, _vp]),
     "jq_ply": (ctypes.c_int, [_PB, _vp, _i32, _PO, _i32, _u64, _u64, _vp, _vp, _i32, _vp, _vp, _vp]),

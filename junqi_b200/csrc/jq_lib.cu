@@ -11,6 +11,7 @@
 #include <atomic>
 #include <mutex>
 
+#include "jq_hist.cuh"
 #include "jq_obs.cuh"
 #include "jq_ply.cuh"
 #include "jq_rules.cuh"
@@ -470,6 +471,33 @@ int jq_ply(const jq_batch *b, const int32_t *d_world_actions, int32_t show_mode,
     a.mask = d_mask;
     a.stats = d_stats;
     return launch_rules(a, (cudaStream_t)stream);
+}
+
+int32_t jq_history_record_bytes(void) { return (int32_t)sizeof(HistRec); }
+
+int jq_history_snapshot(const jq_batch *b, const int8_t *d_seats, void *d_history, int64_t step, int64_t num_steps,
+                        void *stream) {
+    int rc = check_batch(b);
+    if (rc) return rc;
+    if (!d_history || ((uintptr_t)d_history & 15)) return fail(JQ_ERR_ARG, "history must be a 16-byte aligned buffer");
+    if (step < 0 || step >= num_steps) return fail(JQ_ERR_ARG, "step outside [0, num_steps)");
+    hist_snapshot_kernel<<<(b->n + 7) / 8, 256, 0, (cudaStream_t)stream>>>(*b, d_seats, static_cast<HistRec *>(d_history),
+                                                                         (long long)step);
+    CU(cudaGetLastError());
+    return JQ_OK;
+}
+
+int jq_history_restore(const void *d_history, int64_t num_records, const int64_t *d_indices, const jq_batch *scratch,
+                       int8_t *d_observers, void *stream) {
+    int rc = check_batch(scratch);
+    if (rc) return rc;
+    if (!d_history || ((uintptr_t)d_history & 15)) return fail(JQ_ERR_ARG, "history must be a 16-byte aligned buffer");
+    if (!d_indices || !d_observers || num_records < 0) return fail(JQ_ERR_ARG, "indices / observers missing");
+    hist_restore_kernel<<<(scratch->n + 7) / 8, 256, 0, (cudaStream_t)stream>>>(
+        *scratch, static_cast<const HistRec *>(d_history), (long long)num_records,
+        reinterpret_cast<const long long *>(d_indices), d_observers);
+    CU(cudaGetLastError());
+    return JQ_OK;
 }
 
 int jq_legal(const jq_batch *b, const int8_t *d_seats, int32_t *d_counts, int32_t *d_ids, int32_t cap,

@@ -439,3 +439,49 @@ def build_observation_batch_resident(state, obs_out: DeviceObservationBatch, sho
 def build_observation_single_seat(state, obs_out: DeviceObservationSingleBatch, d_acting_seats_ptr: int,
                                   show_mode=2) -> None:
     _observe(state, d_acting_seats_ptr, 1, show_mode, obs_out.d_spatial_ptr, obs_out.d_global_ptr)
+
+
+# ---------------------------------------------------------------------------
+# Rollout history (junqi_cuda.h:186-277, bindings.cpp:728-800)
+# ---------------------------------------------------------------------------
+class DeviceRolloutHistory:
+    """Compact device history that rebuilds PPO minibatches on the device.
+
+    Each record holds what the recorded seat's observation and legal mask
+    read: 12,000 bytes (the reference's record, float beliefs plus all four
+    observers' combat memory, is 47,243 B: rollout_storage.py:48-52).  The
+    observer of a rebuilt record is the seat recorded by ``snapshot``;
+    ``reconstruct``'s acting seats are accepted for compatibility."""
+
+    def __init__(self, num_steps: int, num_envs: int):
+        from .history import RolloutHistory
+        self._h = RolloutHistory(num_steps, num_envs, _device)
+        self.num_steps, self.num_envs = int(num_steps), int(num_envs)
+        self.history_bytes = self._h.history_bytes
+        self.replay_capacity = 0
+
+    def snapshot(self, state: DeviceGameStateBatch, d_acting_seats_ptr: int, step: int) -> None:
+        seats = None
+        if d_acting_seats_ptr:
+            seats = _device_view(d_acting_seats_ptr, state.num_envs, torch.int8, state.b.device)
+        self._h.snapshot(state.b, step, seats)
+
+    def reconstruct(self, d_flat_indices_ptr: int, d_acting_seats_ptr: int, batch_size: int,
+                    show_mode: int = 2) -> dict:
+        idx = _device_view(d_flat_indices_ptr, batch_size, torch.int64, self._h.device).clone()
+        out = self._h.reconstruct(idx, show_mode)
+        self.replay_capacity = max(self.replay_capacity, self._h._cap)
+        return {"d_spatial_ptr": out["spatial"].data_ptr(), "d_global_ptr": out["global"].data_ptr(),
+                "d_legal_mask_ptr": out["mask"].data_ptr(), "batch_size": int(batch_size)}
+
+
+def _device_view(ptr: int, shape, dtype: torch.dtype, device) -> torch.Tensor:
+    """A tensor over caller-owned device memory at `ptr` (no copy)."""
+    shape = (int(shape),) if isinstance(shape, (int, np.integer)) else tuple(int(d) for d in shape)
+    typestr = {torch.int8: "|i1", torch.uint8: "|u1", torch.bool: "|b1", torch.int32: "<i4", torch.int64: "<i8",
+               torch.float32: "<f4"}[dtype]
+
+    class _Arr:
+        __cuda_array_interface__ = {"shape": shape, "typestr": typestr, "data": (int(ptr), False), "version": 3,
+                                    "strides": None}
+    return torch.as_tensor(_Arr(), device=device)

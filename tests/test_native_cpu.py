@@ -98,3 +98,10 @@ def test_entry_points_reject_bad_arguments_without_a_gpu():
     assert L.jq_csr(0, None, None, 0, None, None, None, None) == 1
     assert L.jq_sample_uniform(0, None, None, 0, 0, 0, None, None) == 1
     assert b"bad" in L.jq_last_error() or len(L.jq_last_error()) > 0
+
+
+def test_history_record_is_compact_and_aligned():
+    """One rollout-history record per (step, env): 16-byte aligned, and far
+    smaller than the 366 KB observation it rebuilds."""
+    size = N.lib().jq_history_record_bytes()
+    assert size % 16 == 0 and 8_000 <= size <= 16_384
