@@ -16,7 +16,7 @@
 #include <stddef.h>
 #include <stdint.h>
 
-#define JQ_ABI_VERSION 3
+#define JQ_ABI_VERSION 4
 
 #define JQ_NUM_PIECES 120
 #define JQ_NUM_CELLS 289
@@ -104,6 +104,8 @@ typedef struct jq_step_out {
     uint8_t *flag_captured;
     float *reward;
     int32_t *world_action;   /* filled by jq_step_canonical */
+    int64_t *zobrist;        /* post-step state hash, before any auto-reset
+                                (replay self-check, junqi_core/replay.py:243-260) */
 } jq_step_out;
 
 #ifdef __cplusplus
@@ -155,6 +157,12 @@ int32_t jq_pool_index(uint64_t seed, uint64_t ply, int32_t env, int32_t pool_siz
  * reset_terminated_envs + init_beliefs_for_reset_envs (bindings.cpp:1224-1262). */
 int jq_reset(const jq_batch *b, uint64_t seed, uint64_t ply, int32_t all, int32_t show_mode,
              void *stream);
+
+/* Reset env e to GameState.new_game(pool[d_rows[e]]) (as jq_reset) for every
+ * e with 0 <= d_rows[e] < pool size; other envs are left as they are.  For
+ * replaying recorded games from their own setups (junqi_core/replay.py:
+ * 226-240 starts every replay from new_game(setups)). */
+int jq_reset_rows(const jq_batch *b, const int32_t *d_rows, int32_t show_mode, void *stream);
 
 /* Initial beliefs (BeliefTensor.initial for all four observers,
  * info_model.py:218-270) and an empty move history for every env, for

@@ -50,7 +50,8 @@ RULES_BATCHED, RULES_GAMESTATE = 0, 1
 
 class JqStepOut(ctypes.Structure):
     _fields_ = [(n, ctypes.c_void_p) for n in
-                ("valid", "event", "terminated", "winner", "draw", "flag_captured", "reward", "world_action")]
+                ("valid", "event", "terminated", "winner", "draw", "flag_captured", "reward", "world_action",
+                 "zobrist")]
 
 
 # exported name -> (restype, argtypes)
@@ -67,6 +68,7 @@ SIGNATURES = {
     "jq_set_setup_pool": (ctypes.c_int, [_vp, _i32]),
     "jq_pool_index": (_i32, [_u64, _u64, _i32, _i32]),
     "jq_reset": (ctypes.c_int, [_PB, _u64, _u64, _i32, _i32, _vp]),
+    "jq_reset_rows": (ctypes.c_int, [_PB, _vp, _i32, _vp]),
     "jq_init_beliefs": (ctypes.c_int, [_PB, _i32, _vp]),
     "jq_rehash": (ctypes.c_int, [_PB, _i32, _vp]),
     "jq_legal_slots": (ctypes.c_int, [_PB, _vp, _vp, _vp]),

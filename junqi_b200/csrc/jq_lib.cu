@@ -392,6 +392,17 @@ int jq_reset(const jq_batch *b, uint64_t seed, uint64_t ply, int32_t all, int32_
     return launch_rules(a, (cudaStream_t)stream);
 }
 
+int jq_reset_rows(const jq_batch *b, const int32_t *d_rows, int32_t show_mode, void *stream) {
+    RuleArgs a;
+    int rc = rules_common(a, b, show_mode, true, stream);
+    if (rc) return rc;
+    if (!a.pool) return fail(JQ_ERR_NOT_READY, "setup pool not set");
+    if (!d_rows) return fail(JQ_ERR_ARG, "pool rows missing");
+    a.flags = DO_RESET;
+    a.rows = d_rows;
+    return launch_rules(a, (cudaStream_t)stream);
+}
+
 int jq_init_beliefs(const jq_batch *b, int32_t show_mode, void *stream) {
     RuleArgs a;
     int rc = rules_common(a, b, show_mode, false, stream);

@@ -29,6 +29,7 @@ struct RuleArgs {
     uint8_t *mask;
     int64_t *stats;
     const int8_t *seats;
+    const int32_t *rows;  // explicit pool rows for DO_RESET (NULL: hashed index)
     int flags;
 };
 
@@ -60,12 +61,15 @@ __device__ bool warp_ply_env(const RuleArgs &a, const Topo &T, WEnv &w, int e, i
         __syncwarp();
     }
     if (a.flags & DO_STEP) applied = warp_step(b, T, w, e, lane, a.acts[e], a.mode, a.out, a.stats);
-    if (a.flags & DO_RESET) {
-        const bool do_it = (a.flags & RESET_ALL) || b.terminated[e];
-        if (do_it && a.pool && a.pool_size > 0) {
-            const int8_t *lu = a.pool + (size_t)pool_index(a.seed, a.ply, e, a.pool_size) * NP;
-            warp_reset(b, T, w, e, lane, lu, a.mode);
+    if ((a.flags & DO_RESET) && a.pool && a.pool_size > 0) {
+        int row = -1;
+        if (a.rows) {
+            const int r = a.rows[e];
+            row = (r >= 0 && r < a.pool_size) ? r : -1;
+        } else if ((a.flags & RESET_ALL) || b.terminated[e]) {
+            row = pool_index(a.seed, a.ply, e, a.pool_size);
         }
+        if (row >= 0) warp_reset(b, T, w, e, lane, a.pool + (size_t)row * NP, a.mode);
     }
     __syncwarp();
     if (a.flags & DO_LEGAL) {

@@ -823,6 +823,7 @@ __device__ bool warp_step(const jq_batch &b, const Topo &T, WEnv &w, int e, int 
         if (out.draw) out.draw[e] = (uint8_t)w.s_draw;
         if (out.flag_captured) out.flag_captured[e] = 0;
         if (out.reward) out.reward[e] = 0.f;
+        if (out.zobrist) out.zobrist[e] = w.s_zob;
         if (!term0 && act >= 0 && act < NC * NC) {
             int sf = act / NC, df = act % NC, A = w.cell[sf], D = w.cell[df];
             if (A >= 0 && sf != df) {
@@ -980,6 +981,7 @@ __device__ bool warp_step(const jq_batch &b, const Topo &T, WEnv &w, int e, int 
         if (out.flag_captured) out.flag_captured[e] = (uint8_t)x.fcap;
         if (out.reward)
             out.reward[e] = (x.term && !x.draw && x.win >= 0) ? (((x.acting & 1) == x.win) ? 1.f : -1.f) : 0.f;
+        if (out.zobrist) out.zobrist[e] = zob;
         int hc = w.s_hc;
         b.hist_src[(size_t)e * HIST + (hc & (HIST - 1))] = (int16_t)x.sf;
         b.hist_dst[(size_t)e * HIST + (hc & (HIST - 1))] = (int16_t)x.df;

@@ -72,7 +72,7 @@ class JunqiEnvB200:
         self.out = {k: torch.zeros(n, dtype=dt, device=dev) for k, dt in
                     (("valid", torch.uint8), ("event", torch.int8), ("terminated", torch.uint8),
                      ("winner", torch.int8), ("draw", torch.uint8), ("flag_captured", torch.uint8),
-                     ("reward", torch.float32), ("world_action", torch.int32))}
+                     ("reward", torch.float32), ("world_action", torch.int32), ("zobrist", torch.int64))}
         self._out = N.JqStepOut(**{k: v.data_ptr() for k, v in self.out.items()})
         self.counts = torch.zeros(n, dtype=torch.int32, device=dev)
         self.ids = torch.zeros((n, self.cap), dtype=torch.int32, device=dev)
@@ -106,6 +106,15 @@ class JunqiEnvB200:
         N.check(N.lib().jq_reset(ctypes.byref(self.batch.struct), seed, ply, int(all_envs), self.show_mode,
                                  _stream_ptr()), "jq_reset")
         self.legal()
+
+    def reset_rows(self, rows) -> None:
+        """Reset env e from pool row rows[e] (rows[e] < 0: leave env e as it is); no legal refresh."""
+        r = torch.as_tensor(np.asarray(rows, np.int32) if not torch.is_tensor(rows) else rows, dtype=torch.int32)
+        r = r.to(self.device).contiguous()
+        if r.numel() != self.n:
+            raise ValueError(f"rows: expected {self.n} entries, got {r.numel()}")
+        N.check(N.lib().jq_reset_rows(ctypes.byref(self.batch.struct), r.data_ptr(), self.show_mode, _stream_ptr()),
+                "jq_reset_rows")
 
     def load_state(self, arrays: dict, init_beliefs: bool = True) -> None:
         self.batch.load(arrays)

@@ -192,7 +192,7 @@ class DeviceGameStateBatch:
         self._out = {k: torch.zeros(n, dtype=dt, device=dev) for k, dt in
                      (("valid", torch.uint8), ("event", torch.int8), ("terminated", torch.uint8),
                       ("winner", torch.int8), ("draw", torch.uint8), ("flag_captured", torch.uint8),
-                      ("reward", torch.float32), ("world_action", torch.int32))}
+                      ("reward", torch.float32), ("world_action", torch.int32), ("zobrist", torch.int64))}
         self._out_s = N.JqStepOut(**{k: v.data_ptr() for k, v in self._out.items()})
         self._counts = torch.zeros(n, dtype=torch.int32, device=dev)
         self._ids = torch.zeros((n, MAX_ACTIONS_PER_ENV), dtype=torch.int32, device=dev)
