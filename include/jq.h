@@ -201,6 +201,14 @@ int jq_step_canonical(const jq_batch *b, const int32_t *d_compact_actions,
                       const int8_t *d_seats, int32_t show_mode, const jq_step_out *out,
                       void *stream);
 
+/* Compact canonical actions (cs*129+cd, in the frame of d_seats[e], or of
+ * each env's turn when d_seats is NULL) to world flat ids src*289+dst; -1
+ * for ids outside [0, 16641).  The rotation half of jq_step_canonical, for
+ * callers that step through jq_ply (UNROTATE_LUT, action_lut.py:116-126;
+ * rotate_actions_kernel, game_state.cu:2639-2685). */
+int jq_canonical_to_world(const jq_batch *b, const int32_t *d_compact_actions, const int8_t *d_seats,
+                          int32_t *d_world_actions, void *stream);
+
 /* Fused ply: jq_step, then auto-reset of the envs it terminated (pool
  * index from (seed, ply, env)), then legal generation for the new turn
  * (see jq_legal).  d_world_actions may be NULL to skip the step.  When

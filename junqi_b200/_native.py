@@ -69,6 +69,7 @@ SIGNATURES = {
     "jq_pool_index": (_i32, [_u64, _u64, _i32, _i32]),
     "jq_reset": (ctypes.c_int, [_PB, _u64, _u64, _i32, _i32, _vp]),
     "jq_reset_rows": (ctypes.c_int, [_PB, _vp, _i32, _vp]),
+    "jq_canonical_to_world": (ctypes.c_int, [_PB, _vp, _vp, _vp, _vp]),
     "jq_init_beliefs": (ctypes.c_int, [_PB, _i32, _vp]),
     "jq_rehash": (ctypes.c_int, [_PB, _i32, _vp]),
     "jq_legal_slots": (ctypes.c_int, [_PB, _vp, _vp, _vp]),

@@ -462,6 +462,17 @@ int jq_step_canonical(const jq_batch *b, const int32_t *d_compact_actions, const
     return jq_step(b, out->world_action, show_mode, out, stream);
 }
 
+int jq_canonical_to_world(const jq_batch *b, const int32_t *d_compact_actions, const int8_t *d_seats,
+                          int32_t *d_world_actions, void *stream) {
+    int rc = check_batch(b);
+    if (rc) return rc;
+    if (!d_compact_actions || !d_world_actions) return fail(JQ_ERR_ARG, "actions missing");
+    rotate_actions_kernel<<<(b->n + 255) / 256, 256, 0, (cudaStream_t)stream>>>(b->n, d_compact_actions, d_seats,
+                                                                             b->turn, d_world_actions);
+    CU(cudaGetLastError());
+    return JQ_OK;
+}
+
 int jq_ply(const jq_batch *b, const int32_t *d_world_actions, int32_t show_mode, const jq_step_out *out,
            int32_t autoreset, uint64_t seed, uint64_t ply, int32_t *d_counts, int32_t *d_ids, int32_t cap,
            uint8_t *d_mask, int64_t *d_stats, void *stream) {
