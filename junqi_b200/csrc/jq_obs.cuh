@@ -4,37 +4,44 @@
 // (366,452 B) plus 28 globals, almost all zeros or ones.
 //
 // A unit is first described in shared memory as a bitstream with one bit per
-// output float in output order (the float is 1.0, else 0.0) plus a list of
-// exceptions -- (float index, value) for every float holding another value
-// (belief probability, kill count / 3, recency, progress, -1 of a history
-// source), about a thousand per unit.  The stream starts 4 - head bits in,
-// where head (0..3) is the number of floats before the unit's first 16-byte
-// boundary in global memory (a unit is 91,613 floats, so its base is only
-// 4-byte aligned); every aligned float4 of the output then owns one 4-bit
-// nibble of a 32-bit word.
+// output float in output order (the float is 1.0, else 0.0), plus what the
+// other floats need: one record per piece (cell, belief code, direct-combat
+// pid set, recency values), the two progress constants, and an exception
+// list (float index, value) for the -1 of each history source.  The stream
+// starts 4 - head bits in, where head (0..3) is the number of floats before
+// the unit's first 16-byte boundary in global memory (a unit is 91,613
+// floats, so its base is only 4-byte aligned); every aligned float4 of the
+// output then owns one 4-bit nibble of a 32-bit word.
 //
 // Persistent CTAs of 12 warps, specialised:
 //  * 4 staging warps take units in memory order through an atomic ticket
-//    and build unit k+1 in one of two shared buffers (thread p sets the bits
-//    piece p lights at its canonical cell with shared atomicOr and appends
-//    its exceptions; then history, constant and board-static planes; the
-//    globals go straight to HBM);
-//  * 8 streaming warps write unit k from the other buffer: warp w one
-//    contiguous slab of the unit's aligned float4s, each float4 one shared
-//    word, a shift, four selects and a 16-byte store -- no branch -- and,
-//    after a barrier among them, the exception list as 4-byte stores over
-//    the lines just written (still in L2).
+//    (two units ahead, so the next unit's state lines are prefetched into
+//    L2 while this one is staged) and build unit k+1 in one of two shared
+//    buffers: warp w takes the 30 pieces of seat o + w, thread = piece,
+//    setting the bits the piece lights at its canonical cell with shared
+//    atomicOr and filling its record; then history, constant and
+//    board-static planes; the globals go straight to HBM;
+//  * 8 streaming warps write unit k from the other buffer: pass 1, warp w
+//    one contiguous slab of the unit's aligned float4s, each float4 one
+//    shared word, a shift, four selects and a 16-byte store -- no branch;
+//    pass 2, after a barrier among them, over lines still in L2: belief
+//    values, kill counts / 3 and recency from the piece records, the
+//    progress planes, the exceptions; then they clear the bitstream.
 // Named barriers hand the buffers back and forth (full / empty per buffer),
-// so staging latency -- dependent global loads per piece -- hides behind
-// the previous unit's stream.  Taking units in memory order keeps the units
-// being written at any moment in one compact window of the output: CTAs
-// that drift apart under a static unit-per-CTA stride spread the dirty
-// lines over the whole buffer and lose about a quarter of the DRAM write
-// bandwidth (write microbenchmark on this GPU).
+// so staging hides behind the previous unit's stream.  Taking units in
+// memory order keeps the units being written at any moment in one compact
+// window of the output: CTAs that drift apart under a static unit-per-CTA
+// stride spread the dirty lines over the whole buffer and lose about a
+// quarter of the DRAM write bandwidth (write microbenchmark on this GPU).
+// The value-carrying floats are expanded by the streaming warps rather than
+// queued by the staging warps because staging, not the stream, bounded the
+// kernel: one shared-atomic append per belief value cost more than the
+// whole record expansion.
 //
 // Values go straight to their canonical cell (the observer's rotation
 // applied per cell), which equals the reference's world-frame build
-// followed by rotate_planes.  Every output byte is written once.
+// followed by rotate_planes.  Every output byte is written once, except
+// that pass 2 overwrites the zeros pass 1 left at value-carrying floats.
 #pragma once
 #include "jq_rules.cuh"
 
@@ -54,40 +61,40 @@ constexpr int BAR_FULL0 = 1, BAR_EMPTY0 = 3, BAR_STAGE = 5, BAR_STREAM = 6;
 #define OBS_MIN_CTAS 2
 #endif
 
-// plane kinds (which value an exception float of the plane takes)
-enum : uint8_t { K_BIN = 0, K_CONST = 1, K_HIST = 2, K_BEL = 3, K_KILL = 4, K_REC = 5 };
+// Exceptions per unit: the -1 of each history source.  Every other float
+// that is neither 0 nor 1 comes from a per-piece record (below) or a
+// per-plane constant that the streaming warps expand themselves.
+constexpr int EXC_MAX = HIST;
 
-__host__ __device__ constexpr uint8_t plane_kind(int ch) {
-    return (ch >= 12 && ch < 24) || (ch >= 27 && ch < 51) ? K_BEL
-           : (ch >= 51 && ch < 58) || ch == 64 || ch == 65 ? K_CONST
-           : (ch >= 129 && ch < 161)                        ? K_HIST
-           : (ch >= 211 && ch < 223)                        ? K_KILL
-           : (ch >= 253 && ch < 257)                        ? K_REC
-                                                            : K_BIN;
-}
-
-// Exceptions per unit, upper bound: beliefs 90 x 12, kill counts 60 x 12,
-// recency 60 x 4, progress 2 x 289, history 32.
-constexpr int EXC_MAX = 90 * 12 + 60 * 12 + 60 * 4 + 2 * NC + HIST;  // 2,650
+// Pass-2 work items per unit: belief values (120 pieces x 12 types), kill
+// counts and recency (120 x 16, enemy pieces only), progress planes (2 x 289).
+constexpr int P2_BEL = NP * 12, P2_CM = NP * 16, P2_PROG = 2 * NC;
 
 // One staged unit.
 struct __align__(16) UnitBuf {
     uint32_t bits[OBS_WORDS4 * 4];
-    int32_t exc_pos[EXC_MAX];  // output float index of each exception
+    uint64_t pdlo[NP], pdhi[NP];        // enemy piece: its direct-combat pid set (kill-count planes 211-222)
+    uint64_t type_lo[12], type_hi[12];  // observer-own pids of each tracked type
+    float prec[NP][4];                  // enemy piece: recency planes 253-256 (0: none)
+    int16_t pcell[NP];                  // canonical cell of an alive on-board piece, -1: none
+    uint8_t pflag[NP];                  // bit 0: belief record, bit 1: combat-memory record
+    uint8_t pbase[NP], pcode[NP];       // belief record: first plane (12 / 27 / 39) and belief code
+    int32_t exc_pos[EXC_MAX];           // output float index of each exception
     float exc_val[EXC_MAX];
-    float cval[2];             // progress planes 64, 65
+    float cval[2];                      // progress planes 64, 65
     int exc_n;
-    int u;                     // unit index, -1: no more units
+    int u;  // unit index, -1: no more units
+    int o;  // its observer
 };
 
 struct __align__(16) ObsSmem {
     UnitBuf buf[2];
-    uint64_t type_lo[12], type_hi[12];  // observer-own pids of each tracked type (staging only)
-    int16_t rotf[NC];                   // world flat -> canonical flat for the staged observer
+    int16_t rotf[4][NC];                // world flat -> canonical flat, per observer seat
     uint16_t stat[STAT_MAX];            // board-static bits: (plane - 58) * 289 + world flat
     int stat_n;
-    int ticket, next_o;   // next unit for the staging warps and its observer
-    uint8_t kind[OBS_CH + 3];
+    int ticket[2], next_o[2];  // the staging warps' next two units and their observers
+    float prior[30 * 12], uniform[12];  // belief tables: global loads here would wait behind the write stream
+    int8_t slot_ch[30];
 };
 
 __device__ __forceinline__ void bar_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
@@ -103,10 +110,10 @@ __device__ __forceinline__ bool in_back_two(int seat, int zx, int zy) {
     return false;
 }
 
-__device__ __forceinline__ float bel_value(int code, int t) {
+__device__ __forceinline__ float bel_value(const float *prior, const float *uniform, int code, int t) {
     if (code >= 1 && code <= 12) return code - 1 == t ? 1.f : 0.f;
-    if (code == BC_UNIFORM) return g_uniform[t];
-    if (code >= BC_PRIOR0 && code < BC_PRIOR0 + 30) return g_prior[(code - BC_PRIOR0) * 12 + t];
+    if (code == BC_UNIFORM) return uniform[t];
+    if (code >= BC_PRIOR0 && code < BC_PRIOR0 + 30) return prior[(code - BC_PRIOR0) * 12 + t];
     return 0.f;
 }
 
@@ -117,20 +124,22 @@ __device__ __forceinline__ void set_bit(uint32_t *s, int q) { atomicOr(&s[q >> 5
 struct Stager {
     UnitBuf &B;
     int qoff;
+    const int16_t *rotf;  // the observer's world -> canonical cell map
     __device__ __forceinline__ int q(int ch, int cell) const { return ch * NC + cell + qoff; }
     __device__ __forceinline__ void one(int ch, int cell) { set_bit(B.bits, q(ch, cell)); }
     __device__ __forceinline__ void exception(int j, float v) {
-        const int i = atomicAdd(&B.exc_n, 1);
+        // one shared atomic per group of converged lanes: a staging warp
+        // works on one seat's pieces, so its lanes mostly append together
+        const unsigned act = __activemask();
+        const int lane = threadIdx.x & 31, leader = __ffs(act) - 1;
+        int base = 0;
+        if (lane == leader) base = atomicAdd(&B.exc_n, __popc(act));
+        base = __shfl_sync(act, base, leader);
+        const int i = base + __popc(act & ((1u << lane) - 1u));
         if (i < EXC_MAX) {
             B.exc_pos[i] = j;
             B.exc_val[i] = v;
         }
-    }
-    // a float with value v (0 leaves it at 0, 1 is a plain bit, anything else an exception)
-    __device__ __forceinline__ void value(int ch, int cell, float v) {
-        if (v == 0.f) return;
-        if (v == 1.f) one(ch, cell);
-        else exception(ch * NC + cell, v);
     }
     __device__ __forceinline__ void ones(int ch0, uint32_t m, int cell) {
         while (m) {
@@ -199,6 +208,19 @@ __device__ void stage_piece(const jq_batch &b, int e, int o, int mode, const Obs
         last_f = b.cm_rank_floor_step[k];
     }
     const int cur = b.move_counter[e];
+    // recency values (observation.py:1556-1562): the table lives in global
+    // memory, so the four loads are issued here, long before their use
+    float recv[4] = {0.f, 0.f, 0.f, 0.f};
+    if (enemy_pid && alive_raw) {
+        const int lasts[4] = {last_d, last_d, last_c, last_f};
+#pragma unroll
+        for (int pl = 0; pl < 4; ++pl)
+            if (lasts[pl] >= 0) {
+                int el = cur - lasts[pl];
+                el = el < 0 ? 0 : (el > RECENCY_LEN - 1 ? RECENCY_LEN - 1 : el);
+                recv[pl] = g_recency[pl * RECENCY_LEN + el];
+            }
+    }
     // the observer's own pieces (pids o*30 .. o*30+29, one warp-aligned group
     // of lanes) also read the opponents' view of them and their eaten-by sets
     const bool own_pid = (p / 30) == o;
@@ -217,9 +239,11 @@ __device__ void stage_piece(const jq_batch &b, int e, int o, int mode, const Obs
 
     const int team = s >= 0 ? (s & 1) : 1;  // numpy _SEAT_TEAM[-1] is EAST's team
     int cell;
+    st.B.pcell[p] = -1;
     if (alive_raw) {
         if (!(x >= 0 && x < 17 && y >= 0 && y < 17)) return;
-        cell = S.rotf[y * 17 + x];
+        cell = st.rotf[y * 17 + x];
+        st.B.pcell[p] = (int16_t)cell;
         const int ti = tracked_idx(ptype);
         if (s == o && ti >= 0) st.one(ti, cell);
         int base = -1;
@@ -229,14 +253,18 @@ __device__ void stage_piece(const jq_batch &b, int e, int o, int mode, const Obs
         }
         if (s == left) { st.one(25, cell); base = 27; }
         if (s == right) { st.one(26, cell); base = 39; }
-        if (base >= 0)
-            for (int t = 0; t < 12; ++t) st.value(base + t, cell, bel_value(code, t));
+        uint32_t flag = 0;
+        if (base >= 0) {  // belief planes: expanded from this record by the streaming warps
+            flag = 1;
+            st.B.pbase[p] = (uint8_t)base;
+            st.B.pcode[p] = (uint8_t)code;
+        }
         const int half = team == oteam ? 0 : 4;
         st.one(66 + half + (mcnt < 3 ? mcnt : 3), cell);
         const int ae = ae_raw < 3 ? ae_raw : 3, ps = ps_raw < 3 ? ps_raw : 3;
         st.ones(74 + half, thresh_mask(ae + 1, 4), cell);
         st.ones(82 + half, thresh_mask(ps + 1, 4), cell);
-        const int sch = g_topo.slot_ch[p % 30];
+        const int sch = S.slot_ch[p % 30];
         st.one(104 + (sch < 0 ? 24 : sch), cell);
         if (team != oteam) {
             // layer 1 + 3 (observation.py:1295-1392, 1474-1569)
@@ -251,22 +279,13 @@ __device__ void stage_piece(const jq_batch &b, int e, int o, int mode, const Obs
             if (not_g) st.one(204, cell);
             if (in_back_two(s, zx, zy) && mcnt == 0 && !atk_g) st.one(205, cell);
             st.ones(223, pid_field30(dlo, dhi, o * 30), cell);
-            for (int t = 0; t < 12; ++t) {
-                const int c = __popcll(dlo & S.type_lo[t]) + __popcll(dhi & S.type_hi[t]);
-                if (c) st.value(211 + t, cell, __fdiv_rn((float)(c < 3 ? c : 3), 3.0f));
-            }
-            const int lasts[4] = {last_d, last_d, last_c, last_f};
-#pragma unroll
-            for (int pl = 0; pl < 4; ++pl) {
-                float r = 0.f;
-                if (lasts[pl] >= 0) {
-                    int el = cur - lasts[pl];
-                    el = el < 0 ? 0 : (el > RECENCY_LEN - 1 ? RECENCY_LEN - 1 : el);
-                    r = g_recency[pl * RECENCY_LEN + el];
-                }
-                if (r > 0.f) st.value(253 + pl, cell, r);
-            }
+            // kill-count and recency planes: expanded from this record
+            flag |= 2;
+            st.B.pdlo[p] = dlo;
+            st.B.pdhi[p] = dhi;
+            *reinterpret_cast<float4 *>(st.B.prec[p]) = make_float4(recv[0], recv[1], recv[2], recv[3]);
         }
+        st.B.pflag[p] = (uint8_t)flag;
         if (s == o) {  // layer 2 (observation.py:1394-1459)
             st.ones(206, thresh_mask(lc < rc ? lc : rc, 3), cell);
             if (lg) st.one(209, cell);
@@ -281,11 +300,11 @@ __device__ void stage_piece(const jq_batch &b, int e, int o, int mode, const Obs
                 int yy = dloc >= 0 ? dloc / 17 : -((-dloc + 16) / 17);
                 const int xx = ((dloc % 17) + 17) % 17;
                 if (yy < 0) yy += 17;
-                if (yy >= 0 && yy < 17) st.one(90 + grp + ridx, S.rotf[yy * 17 + xx]);
+                if (yy >= 0 && yy < 17) st.one(90 + grp + ridx, st.rotf[yy * 17 + xx]);
             }
         }
         if (!(zx >= 0 && zx < 17 && zy >= 0 && zy < 17)) return;
-        cell = S.rotf[zy * 17 + zx];
+        cell = st.rotf[zy * 17 + zx];
         if (dstep != -1) st.one(102 + (team == oteam ? 0 : 1), cell);
     }
     if (own_pid) {  // layer 4: observer-own pid at its cell (alive) or zero cell (dead)
@@ -310,18 +329,56 @@ __device__ __forceinline__ int unit_observer(const jq_batch &b, const int8_t *ob
     return (observers ? observers[u] : (seats == 1 ? b.turn[e] : u % seats)) & 3;
 }
 
+__device__ __forceinline__ void prefetch_l2(const void *ptr) {
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(ptr));
+}
+
+// Pull the state lines unit u (observer o) will read into L2 while the
+// current unit is staged: under the full-bandwidth write stream a load that
+// misses L2 waits thousands of cycles, and staging is a few rounds of
+// dependent loads.  Thread t covers the fields of the piece it will stage.
+__device__ void prefetch_unit(const jq_batch &b, int seats, int u, int o, int t) {
+    const int e = u / seats, w = t >> 5, ln = t & 31;
+    if (ln < 30) {
+        const int p = ((o + w) & 3) * 30 + ln;
+        const size_t q = PI(e, p), k = OI(e, o, p);
+        prefetch_l2(b.alive + q); prefetch_l2(b.piece_seat + q); prefetch_l2(b.pos_x + q);
+        prefetch_l2(b.pos_y + q); prefetch_l2(b.zero_x + q); prefetch_l2(b.zero_y + q);
+        prefetch_l2(b.piece_type + q); prefetch_l2(b.move_count + q); prefetch_l2(b.active_eat + q);
+        prefetch_l2(b.passive_surv + q); prefetch_l2(b.death_step + q); prefetch_l2(b.death_reason + q);
+        prefetch_l2(b.death_loc + q); prefetch_l2(b.bel_code + k);
+        if (w & 1) {  // an enemy seat: the observer's combat-memory row of the piece
+            prefetch_l2(b.cm_direct_lo + k); prefetch_l2(b.cm_direct_hi + k); prefetch_l2(b.cm_chain_lo + k);
+            prefetch_l2(b.cm_chain_hi + k); prefetch_l2(b.cm_direct_type + k); prefetch_l2(b.cm_chain_type + k);
+            prefetch_l2(b.cm_direct_other + k); prefetch_l2(b.cm_rank_floor + k); prefetch_l2(b.cm_is_gongb + k);
+            prefetch_l2(b.cm_not_gongb + k); prefetch_l2(b.cm_atk_gongb + k);
+            prefetch_l2(b.cm_last_direct_step + k); prefetch_l2(b.cm_last_chain_step + k);
+            prefetch_l2(b.cm_rank_floor_step + k);
+        } else if (w == 0) {  // the observer's own pieces: the opponents' views and eaten-by sets
+            const size_t kl = OI(e, (o + 1) & 3, p), kr = OI(e, (o + 3) & 3, p);
+            prefetch_l2(b.cm_direct_lo + kl); prefetch_l2(b.cm_direct_hi + kl); prefetch_l2(b.cm_direct_other + kl);
+            prefetch_l2(b.cm_is_gongb + kl); prefetch_l2(b.cm_atk_gongb + kl);
+            prefetch_l2(b.cm_direct_lo + kr); prefetch_l2(b.cm_direct_hi + kr); prefetch_l2(b.cm_direct_other + kr);
+            prefetch_l2(b.cm_is_gongb + kr); prefetch_l2(b.cm_atk_gongb + kr);
+            prefetch_l2(b.cm_eaten_lo + k); prefetch_l2(b.cm_eaten_hi + k);
+        }
+    } else if (w == 0) {  // per-env rows
+        if (ln == 30) {
+            prefetch_l2(b.move_counter + e); prefetch_l2(b.mslc + e); prefetch_l2(b.hist_count + e);
+            prefetch_l2(b.seat_dead + (size_t)e * 4); prefetch_l2(b.seat_flag + (size_t)e * 4);
+        } else {
+            prefetch_l2(b.hist_src + (size_t)e * HIST); prefetch_l2(b.hist_dst + (size_t)e * HIST);
+            prefetch_l2(b.remaining + (size_t)e * 192 + o * 48);
+            prefetch_l2(b.remaining + (size_t)e * 192 + o * 48 + 47);
+        }
+    }
+}
+
 __device__ void stage_unit(const jq_batch &b, int seats, int mode, float *global, ObsSmem &S, UnitBuf &B, int u,
                            int o, int head, int t, int bar_stage) {
     const int e = u / seats;
     const int tm = (o + 2) & 3, left = (o + 1) & 3, right = (o + 3) & 3;
-    Stager st{B, 4 - head};
-    // init
-    {
-        uint4 *b4 = reinterpret_cast<uint4 *>(B.bits);
-        const uint4 z = make_uint4(0u, 0u, 0u, 0u);
-        for (int k2 = t; k2 < OBS_WORDS4; k2 += OBS_STAGE_THREADS) b4[k2] = z;
-    }
-    for (int f = t; f < NC; f += OBS_STAGE_THREADS) S.rotf[f] = g_topo.rotf[o][f];
+    Stager st{B, 4 - head, S.rotf[o]};  // B.bits arrive zeroed by the streaming warps
     if (t < 32) {  // observer-own pids per tracked type: one load per lane, one ballot per type
         const int ti = t < 30 ? tracked_idx(b.piece_type[PI(e, o * 30 + t)]) : -1;
         const int pos = o * 30;
@@ -329,8 +386,8 @@ __device__ void stage_unit(const jq_batch &b, int seats, int mode, float *global
         for (int tt = 0; tt < 12; ++tt) {
             const uint64_t m = __ballot_sync(0xffffffffu, ti == tt) & 0x3FFFFFFFu;
             if (t == tt) {
-                S.type_lo[tt] = pos < 64 ? m << pos : 0ull;
-                S.type_hi[tt] = pos >= 64 ? m << (pos - 64) : (pos + 30 > 64 ? m >> (64 - pos) : 0ull);
+                B.type_lo[tt] = pos < 64 ? m << pos : 0ull;
+                B.type_hi[tt] = pos >= 64 ? m << (pos - 64) : (pos + 30 > 64 ? m >> (64 - pos) : 0ull);
             }
         }
     }
@@ -349,18 +406,22 @@ __device__ void stage_unit(const jq_batch &b, int seats, int mode, float *global
     }
     if (t == 0) {
         B.u = u;
+        B.o = o;
         B.exc_n = 0;
     }
     bar_sync(bar_stage, OBS_STAGE_THREADS);
     // pieces, then history / constants / statics (all bit writes are atomic)
-    if (t < NP) stage_piece(b, e, o, mode, S, st, t);
+    {  // staging warp w takes the 30 pieces of seat o + w: one seat relation per warp
+        const int ln = t & 31;
+        if (ln < 30) stage_piece(b, e, o, mode, S, st, ((o + (t >> 5)) & 3) * 30 + ln);
+    }
     if (t < HIST) {  // move history (observation.py:1207-1231)
         const int hc = b.hist_count[e], n = hc < HIST ? hc : HIST;
         if (t < n) {
             const int slot = (hc - 1 - t) & (HIST - 1);
             const int s = b.hist_src[(size_t)e * HIST + slot], d = b.hist_dst[(size_t)e * HIST + slot];
             if (s >= 0 && s < NC && d >= 0 && d < NC) {
-                const int cs = S.rotf[s], cd = S.rotf[d];
+                const int cs = st.rotf[s], cd = st.rotf[d];
                 st.one(129 + t, cd);
                 if (cs != cd) st.exception((129 + t) * NC + cs, -1.f);  // the destination's +1 wins
             }
@@ -382,22 +443,17 @@ __device__ void stage_unit(const jq_batch &b, int seats, int mode, float *global
             const uint32_t on = ((j < 3 ? dead4 : flag4) >> sd) & 1u;
             if (on) st.fill_plane(B.bits, 51 + j, k, nk);
         }
-        for (int j = 0; j < 2; ++j) {
-            const float v = B.cval[j];
-            if (v == 1.f) st.fill_plane(B.bits, 64 + j, k, nk);
-            else if (v != 0.f)
-                for (int c = k; c < NC; c += nk) st.exception((64 + j) * NC + c, v);
-        }
         for (int i = k; i < S.stat_n; i += nk) {
             const int en = S.stat[i], pl = en / NC, f = en - pl * NC;
-            st.one(58 + pl, S.rotf[f]);
+            st.one(58 + pl, st.rotf[f]);
         }
     }
 }
 
 // Streaming warps: write unit B.u.  w = streaming warp 0..nwarps-1, t = its thread;
 // bar_stream is a named barrier of the nwarps streaming warps.
-__device__ void stream_unit(const UnitBuf &B, float *spatial, int w, int lane, int nwarps, int bar_stream) {
+__device__ void stream_unit(UnitBuf &B, const float *prior, const float *uniform, float *spatial, int w, int lane,
+                            int nwarps, int bar_stream) {
     const int u = B.u, t = w * 32 + lane;
     float *out = spatial + (size_t)u * OBS_FLOATS;
     const int head = unit_head(spatial, u), qoff = 4 - head;
@@ -419,10 +475,41 @@ __device__ void stream_unit(const UnitBuf &B, float *spatial, int w, int lane, i
         out4[g] = make_float4((nib & 1u) ? 1.f : 0.f, (nib & 2u) ? 1.f : 0.f, (nib & 4u) ? 1.f : 0.f,
                               (nib & 8u) ? 1.f : 0.f);
     }
-    // pass 2: the exceptions, ordered after pass 1 by the streaming warps' barrier
+    // pass 2, ordered after pass 1 by the streaming warps' barrier: the
+    // floats that are neither 0 nor 1, over lines still in L2 -- exceptions,
+    // then the values the per-piece records and the progress constants
+    // expand to (observation.py:937-962, 1014-1021, 1541-1562); then the
+    // bitstream is cleared for the unit staged next in B
     bar_sync(bar_stream, 32 * nwarps);
+    const int nthr = 32 * nwarps;
     const int n = B.exc_n < EXC_MAX ? B.exc_n : EXC_MAX;
-    for (int i = t; i < n; i += 32 * nwarps) out[B.exc_pos[i]] = B.exc_val[i];
+    for (int i = t; i < n; i += nthr) out[B.exc_pos[i]] = B.exc_val[i];
+    // items are plane-major (consecutive threads: consecutive pieces, one
+    // plane), so a warp's stores fall on a few lines of one plane
+    for (int i = t; i < P2_BEL; i += nthr) {
+        const int k = i / NP, p = i - k * NP, cell = B.pcell[p];
+        if (cell < 0 || !(B.pflag[p] & 1)) continue;
+        const float v = bel_value(prior, uniform, B.pcode[p], k);
+        if (v != 0.f) out[(B.pbase[p] + k) * NC + cell] = v;
+    }
+    for (int i = t; i < P2_CM; i += nthr) {
+        const int k = i / NP, p = i - k * NP, cell = B.pcell[p];
+        if (cell < 0 || !(B.pflag[p] & 2)) continue;
+        if (k < 12) {
+            const int c = __popcll(B.pdlo[p] & B.type_lo[k]) + __popcll(B.pdhi[p] & B.type_hi[k]);
+            if (c) out[(211 + k) * NC + cell] = __fdiv_rn((float)(c < 3 ? c : 3), 3.0f);
+        } else {
+            const float r = B.prec[p][k - 12];
+            if (r > 0.f) out[(253 + k - 12) * NC + cell] = r;
+        }
+    }
+    for (int i = t; i < P2_PROG; i += nthr) {
+        const int j = i >= NC ? 1 : 0;
+        const float v = B.cval[j];
+        if (v != 0.f) out[(64 + j) * NC + i - j * NC] = v;
+    }
+    uint4 *b4 = reinterpret_cast<uint4 *>(B.bits);
+    for (int k = t; k < OBS_WORDS4; k += nthr) b4[k] = make_uint4(0u, 0u, 0u, 0u);
 }
 
 // Grid: persistent.  ticket[0] hands out units u = e * seats + k in order;
@@ -435,7 +522,12 @@ __global__ void __launch_bounds__(OBS_THREADS, OBS_MIN_CTAS) obs_kernel(jq_batch
     ObsSmem &S = *reinterpret_cast<ObsSmem *>(smem_raw);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     // once per CTA: plane kinds and the list of board-static bits (observation.py:343-383)
-    for (int ch = tid; ch < OBS_CH + 3; ch += OBS_THREADS) S.kind[ch] = ch < OBS_CH ? plane_kind(ch) : K_BIN;
+    for (int i = tid; i < 4 * NC; i += OBS_THREADS) (&S.rotf[0][0])[i] = (&g_topo.rotf[0][0])[i];
+    for (int i = tid; i < 30 * 12; i += OBS_THREADS) S.prior[i] = g_prior[i];
+    if (tid < 12) S.uniform[tid] = g_uniform[tid];
+    if (tid < 30) S.slot_ch[tid] = g_topo.slot_ch[tid];
+    for (int i = tid; i < 2 * OBS_WORDS4; i += OBS_THREADS)
+        reinterpret_cast<uint4 *>(S.buf[i / OBS_WORDS4].bits)[i % OBS_WORDS4] = make_uint4(0u, 0u, 0u, 0u);
     if (tid == 0) S.stat_n = 0;
     __syncthreads();
     for (int f = tid; f < NC; f += OBS_THREADS) {
@@ -453,9 +545,9 @@ __global__ void __launch_bounds__(OBS_THREADS, OBS_MIN_CTAS) obs_kernel(jq_batch
         for (int k = 0;; ++k) {
             const int bi = k & 1;
             bar_sync(BAR_FULL0 + bi, OBS_THREADS);  // buffer bi staged
-            const UnitBuf &B = S.buf[bi];
+            UnitBuf &B = S.buf[bi];
             if (B.u < 0) break;
-            stream_unit(B, spatial, warp, lane, OBS_STREAM_WARPS, BAR_STREAM);
+            stream_unit(B, S.prior, S.uniform, spatial, warp, lane, OBS_STREAM_WARPS, BAR_STREAM);
             bar_arrive(BAR_EMPTY0 + bi, OBS_THREADS);  // buffer bi free again
         }
     } else {
@@ -463,12 +555,15 @@ __global__ void __launch_bounds__(OBS_THREADS, OBS_MIN_CTAS) obs_kernel(jq_batch
         // The next unit (and its observer) is fetched while the current one
         // is staged, so the ticket and observer loads leave the critical path.
         if (t == 0) {
-            const int u0 = atomicAdd(&ticket[0], 1);
-            S.ticket = u0;
-            S.next_o = u0 < units ? unit_observer(b, observers, seats, u0) : 0;
+            const int u0 = atomicAdd(&ticket[0], 2);
+            S.ticket[0] = u0;
+            S.next_o[0] = u0 < units ? unit_observer(b, observers, seats, u0) : 0;
+            S.ticket[1] = u0 + 1;
+            S.next_o[1] = u0 + 1 < units ? unit_observer(b, observers, seats, u0 + 1) : 0;
         }
         bar_sync(BAR_STAGE, OBS_STAGE_THREADS);
-        int u = S.ticket, o = S.next_o;
+        int u = S.ticket[0], o = S.next_o[0], u1 = S.ticket[1], o1 = S.next_o[1];
+        if (u1 < units) prefetch_unit(b, seats, u1, o1, t);
         int k = 0;
         for (;; ++k) {
             const int bi = k & 1;
@@ -485,10 +580,13 @@ __global__ void __launch_bounds__(OBS_THREADS, OBS_MIN_CTAS) obs_kernel(jq_batch
                 on = un < units ? unit_observer(b, observers, seats, un) : 0;
             }
             stage_unit(b, seats, mode, global, S, B, u, o, unit_head(spatial, u), t, BAR_STAGE);
-            if (t == 0) { S.ticket = un; S.next_o = on; }
-            bar_sync(BAR_STAGE, OBS_STAGE_THREADS);  // unit staged; next ticket published
-            u = S.ticket;
-            o = S.next_o;
+            if (t == 0) { S.ticket[0] = un; S.next_o[0] = on; }
+            bar_sync(BAR_STAGE, OBS_STAGE_THREADS);  // unit staged; the ticket after next published
+            u = u1;
+            o = o1;
+            u1 = S.ticket[0];
+            o1 = S.next_o[0];
+            if (u1 < units) prefetch_unit(b, seats, u1, o1, t);
             bar_arrive(BAR_FULL0 + bi, OBS_THREADS);
             bar_sync(BAR_STAGE, OBS_STAGE_THREADS);  // everyone has read the next ticket
         }
