@@ -54,6 +54,10 @@ constexpr int OBS_THREADS = 32 * (OBS_STREAM_WARPS + OBS_STAGE_WARPS);      // 3
 constexpr int OBS_WORDS = (OBS_FLOATS + 8 + 31) / 32;  // 2,864 words per stream
 constexpr int OBS_WORDS4 = (OBS_WORDS + 3) / 4;         // in uint4
 constexpr int STAT_MAX = NB * 5;                        // (static plane, cell) pairs, upper bound
+// The board-static planes 58-62 as stream words: they start in word
+// STAT_W0 for every stream offset 1..4 and span STAT_WORDS words.
+constexpr int STAT_W0 = (58 * NC + 1) >> 5, STAT_WORDS = ((63 * NC + 4) >> 5) - STAT_W0 + 1;
+static_assert(((58 * NC + 4) >> 5) == STAT_W0, "static planes start in one word for every offset");
 // named barriers (0 is __syncthreads)
 constexpr int BAR_FULL0 = 1, BAR_EMPTY0 = 3, BAR_STAGE = 5, BAR_STREAM = 6;
 
@@ -66,9 +70,9 @@ constexpr int BAR_FULL0 = 1, BAR_EMPTY0 = 3, BAR_STAGE = 5, BAR_STREAM = 6;
 // per-plane constant that the streaming warps expand themselves.
 constexpr int EXC_MAX = HIST;
 
-// Pass-2 work items per unit: belief values (120 pieces x 12 types), kill
-// counts and recency (120 x 16, enemy pieces only), progress planes (2 x 289).
-constexpr int P2_BEL = NP * 12, P2_CM = NP * 16, P2_PROG = 2 * NC;
+// Pass-2 work items per unit besides the record expansions (12 per belief
+// record, 16 per combat-memory record): the two progress planes.
+constexpr int P2_PROG = 2 * NC;
 
 // One staged unit.
 struct __align__(16) UnitBuf {
@@ -79,6 +83,8 @@ struct __align__(16) UnitBuf {
     int16_t pcell[NP];                  // canonical cell of an alive on-board piece, -1: none
     uint8_t pflag[NP];                  // bit 0: belief record, bit 1: combat-memory record
     uint8_t pbase[NP], pcode[NP];       // belief record: first plane (12 / 27 / 39) and belief code
+    uint8_t bel_list[NP], cm_list[NP];  // pids holding a belief / combat-memory record
+    int nbel, ncm;
     int32_t exc_pos[EXC_MAX];           // output float index of each exception
     float exc_val[EXC_MAX];
     float cval[2];                      // progress planes 64, 65
@@ -92,6 +98,7 @@ struct __align__(16) ObsSmem {
     int16_t rotf[4][NC];                // world flat -> canonical flat, per observer seat
     uint16_t stat[STAT_MAX];            // board-static bits: (plane - 58) * 289 + world flat
     int stat_n;
+    uint32_t statw[4][4][STAT_WORDS];   // those bits as stream words, per observer and stream offset
     int ticket[2], next_o[2];  // the staging warps' next two units and their observers
     float prior[30 * 12], uniform[12];  // belief tables: global loads here would wait behind the write stream
     int8_t slot_ch[30];
@@ -408,12 +415,28 @@ __device__ void stage_unit(const jq_batch &b, int seats, int mode, float *global
         B.u = u;
         B.o = o;
         B.exc_n = 0;
+        B.nbel = 0;
+        B.ncm = 0;
     }
     bar_sync(bar_stage, OBS_STAGE_THREADS);
     // pieces, then history / constants / statics (all bit writes are atomic)
     {  // staging warp w takes the 30 pieces of seat o + w: one seat relation per warp
         const int ln = t & 31;
-        if (ln < 30) stage_piece(b, e, o, mode, S, st, ((o + (t >> 5)) & 3) * 30 + ln);
+        const int p = ((o + (t >> 5)) & 3) * 30 + ln;
+        if (ln < 30) stage_piece(b, e, o, mode, S, st, p);
+        // list the pieces holding records, one shared atomic per warp and list
+        const bool rec = ln < 30 && B.pcell[p] >= 0;
+        const uint32_t fl = rec ? B.pflag[p] : 0u, below = (1u << ln) - 1u;
+        const uint32_t mb = __ballot_sync(0xffffffffu, fl & 1u), mc = __ballot_sync(0xffffffffu, fl & 2u);
+        int bb = 0, bc = 0;
+        if (ln == 0) {
+            bb = mb ? atomicAdd(&B.nbel, __popc(mb)) : 0;
+            bc = mc ? atomicAdd(&B.ncm, __popc(mc)) : 0;
+        }
+        bb = __shfl_sync(0xffffffffu, bb, 0);
+        bc = __shfl_sync(0xffffffffu, bc, 0);
+        if (fl & 1u) B.bel_list[bb + __popc(mb & below)] = (uint8_t)p;
+        if (fl & 2u) B.cm_list[bc + __popc(mc & below)] = (uint8_t)p;
     }
     if (t < HIST) {  // move history (observation.py:1207-1231)
         const int hc = b.hist_count[e], n = hc < HIST ? hc : HIST;
@@ -443,10 +466,9 @@ __device__ void stage_unit(const jq_batch &b, int seats, int mode, float *global
             const uint32_t on = ((j < 3 ? dead4 : flag4) >> sd) & 1u;
             if (on) st.fill_plane(B.bits, 51 + j, k, nk);
         }
-        for (int i = k; i < S.stat_n; i += nk) {
-            const int en = S.stat[i], pl = en / NC, f = en - pl * NC;
-            st.one(58 + pl, st.rotf[f]);
-        }
+        const uint32_t *sw = S.statw[o][st.qoff - 1];
+        for (int w = k; w < STAT_WORDS; w += nk)
+            if (sw[w]) atomicOr(&B.bits[STAT_W0 + w], sw[w]);
     }
 }
 
@@ -484,17 +506,14 @@ __device__ void stream_unit(UnitBuf &B, const float *prior, const float *uniform
     const int nthr = 32 * nwarps;
     const int n = B.exc_n < EXC_MAX ? B.exc_n : EXC_MAX;
     for (int i = t; i < n; i += nthr) out[B.exc_pos[i]] = B.exc_val[i];
-    // items are plane-major (consecutive threads: consecutive pieces, one
-    // plane), so a warp's stores fall on a few lines of one plane
-    for (int i = t; i < P2_BEL; i += nthr) {
-        const int k = i / NP, p = i - k * NP, cell = B.pcell[p];
-        if (cell < 0 || !(B.pflag[p] & 1)) continue;
+    const int nb = B.nbel * 12, nc = B.ncm * 16;
+    for (int i = t; i < nb; i += nthr) {
+        const int j = i / 12, k = i - j * 12, p = B.bel_list[j];
         const float v = bel_value(prior, uniform, B.pcode[p], k);
-        if (v != 0.f) out[(B.pbase[p] + k) * NC + cell] = v;
+        if (v != 0.f) out[(B.pbase[p] + k) * NC + B.pcell[p]] = v;
     }
-    for (int i = t; i < P2_CM; i += nthr) {
-        const int k = i / NP, p = i - k * NP, cell = B.pcell[p];
-        if (cell < 0 || !(B.pflag[p] & 2)) continue;
+    for (int i = t; i < nc; i += nthr) {
+        const int j = i >> 4, k = i & 15, p = B.cm_list[j], cell = B.pcell[p];
         if (k < 12) {
             const int c = __popcll(B.pdlo[p] & B.type_lo[k]) + __popcll(B.pdhi[p] & B.type_hi[k]);
             if (c) out[(211 + k) * NC + cell] = __fdiv_rn((float)(c < 3 ? c : 3), 3.0f);
@@ -538,6 +557,13 @@ __global__ void __launch_bounds__(OBS_THREADS, OBS_MIN_CTAS) obs_kernel(jq_batch
 #pragma unroll
         for (int i = 0; i < 5; ++i)
             if (fl & fb[i]) S.stat[atomicAdd(&S.stat_n, 1)] = (uint16_t)(i * NC + f);
+    }
+    for (int i = tid; i < 16 * STAT_WORDS; i += OBS_THREADS) (&S.statw[0][0][0])[i] = 0u;
+    __syncthreads();
+    for (int i = tid; i < 16 * S.stat_n; i += OBS_THREADS) {  // every (observer, offset, static bit)
+        const int os = i / S.stat_n, en = S.stat[i - os * S.stat_n], pl = en / NC, f = en - pl * NC;
+        const int q = (58 + pl) * NC + S.rotf[os >> 2][f] + (os & 3) + 1 - STAT_W0 * 32;
+        atomicOr(&S.statw[os >> 2][os & 3][q >> 5], 1u << (q & 31));
     }
     __syncthreads();
     const int units = b.n * seats;
