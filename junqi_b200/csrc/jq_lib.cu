@@ -303,6 +303,11 @@ int jq_init(int device) {
     CU(cudaMemcpyToSymbol(c_topo, &host_topo, sizeof(Topo)));
     CU(cudaMemcpyToSymbol(g_topo, &host_topo, sizeof(Topo)));
     CU(cudaMemcpyToSymbol(g_slot, &host_slot, sizeof(SlotTopo)));
+    {
+        static uint32_t statw[4][4][STAT_WORDS];
+        build_static_words(host_topo, statw);
+        CU(cudaMemcpyToSymbol(g_statw, statw, sizeof(statw)));
+    }
     CU(cudaFuncSetAttribute(rules_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rule_smem()));
     CU(cudaFuncSetAttribute(obs_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)obs_smem()));
     CU(cudaDeviceGetAttribute(&st.sms, cudaDevAttrMultiProcessorCount, device));

@@ -15,8 +15,7 @@
 //
 // Persistent CTAs of 12 warps, specialised:
 //  * 4 staging warps take units in memory order through an atomic ticket
-//    (two units ahead, so the next unit's state lines are prefetched into
-//    L2 while this one is staged) and build unit k+1 in one of two shared
+//    (two units ahead) and build unit k+1 in one of two shared
 //    buffers: warp w takes the 30 pieces of seat o + w, thread = piece,
 //    setting the bits the piece lights at its canonical cell with shared
 //    atomicOr and filling its record; then history, constant and
@@ -53,11 +52,33 @@ constexpr int OBS_STAGE_THREADS = 32 * OBS_STAGE_WARPS;                      // 
 constexpr int OBS_THREADS = 32 * (OBS_STREAM_WARPS + OBS_STAGE_WARPS);      // 384
 constexpr int OBS_WORDS = (OBS_FLOATS + 8 + 31) / 32;  // 2,864 words per stream
 constexpr int OBS_WORDS4 = (OBS_WORDS + 3) / 4;         // in uint4
-constexpr int STAT_MAX = NB * 5;                        // (static plane, cell) pairs, upper bound
 // The board-static planes 58-62 as stream words: they start in word
 // STAT_W0 for every stream offset 1..4 and span STAT_WORDS words.
 constexpr int STAT_W0 = (58 * NC + 1) >> 5, STAT_WORDS = ((63 * NC + 4) >> 5) - STAT_W0 + 1;
 static_assert(((58 * NC + 4) >> 5) == STAT_W0, "static planes start in one word for every offset");
+
+// Built on the host once (build_static_words), copied into each CTA.
+__device__ uint32_t g_statw[4][4][STAT_WORDS];
+
+// The board-static bits (camp, stronghold, rail, nine-grid, arc planes
+// 58-62; observation.py:343-383) for observer o and stream offset s + 1,
+// as stream words from STAT_W0.
+inline void build_static_words(const Topo &T, uint32_t out[4][4][STAT_WORDS]) {
+    const uint8_t fb[5] = {F_CAMP, F_SH, F_RAIL, F_NINE, F_ARC};
+    for (int o = 0; o < 4; ++o)
+        for (int sh = 0; sh < 4; ++sh) {
+            for (int w = 0; w < STAT_WORDS; ++w) out[o][sh][w] = 0u;
+            for (int f = 0; f < NC; ++f) {
+                const int cc = T.f2c[f];
+                if (cc < 0) continue;
+                for (int i = 0; i < 5; ++i)
+                    if (T.flags[cc] & fb[i]) {
+                        const int q = (58 + i) * NC + T.rotf[o][f] + sh + 1 - STAT_W0 * 32;
+                        out[o][sh][q >> 5] |= 1u << (q & 31);
+                    }
+            }
+        }
+}
 // named barriers (0 is __syncthreads)
 constexpr int BAR_FULL0 = 1, BAR_EMPTY0 = 3, BAR_STAGE = 5, BAR_STREAM = 6;
 
@@ -96,9 +117,7 @@ struct __align__(16) UnitBuf {
 struct __align__(16) ObsSmem {
     UnitBuf buf[2];
     int16_t rotf[4][NC];                // world flat -> canonical flat, per observer seat
-    uint16_t stat[STAT_MAX];            // board-static bits: (plane - 58) * 289 + world flat
-    int stat_n;
-    uint32_t statw[4][4][STAT_WORDS];   // those bits as stream words, per observer and stream offset
+    uint32_t statw[4][4][STAT_WORDS];   // board-static bits as stream words, per observer and stream offset
     int ticket[2], next_o[2];  // the staging warps' next two units and their observers
     float prior[30 * 12], uniform[12];  // belief tables: global loads here would wait behind the write stream
     int8_t slot_ch[30];
@@ -336,51 +355,6 @@ __device__ __forceinline__ int unit_observer(const jq_batch &b, const int8_t *ob
     return (observers ? observers[u] : (seats == 1 ? b.turn[e] : u % seats)) & 3;
 }
 
-__device__ __forceinline__ void prefetch_l2(const void *ptr) {
-    asm volatile("prefetch.global.L2 [%0];" ::"l"(ptr));
-}
-
-// Pull the state lines unit u (observer o) will read into L2 while the
-// current unit is staged: under the full-bandwidth write stream a load that
-// misses L2 waits thousands of cycles, and staging is a few rounds of
-// dependent loads.  Thread t covers the fields of the piece it will stage.
-__device__ void prefetch_unit(const jq_batch &b, int seats, int u, int o, int t) {
-    const int e = u / seats, w = t >> 5, ln = t & 31;
-    if (ln < 30) {
-        const int p = ((o + w) & 3) * 30 + ln;
-        const size_t q = PI(e, p), k = OI(e, o, p);
-        prefetch_l2(b.alive + q); prefetch_l2(b.piece_seat + q); prefetch_l2(b.pos_x + q);
-        prefetch_l2(b.pos_y + q); prefetch_l2(b.zero_x + q); prefetch_l2(b.zero_y + q);
-        prefetch_l2(b.piece_type + q); prefetch_l2(b.move_count + q); prefetch_l2(b.active_eat + q);
-        prefetch_l2(b.passive_surv + q); prefetch_l2(b.death_step + q); prefetch_l2(b.death_reason + q);
-        prefetch_l2(b.death_loc + q); prefetch_l2(b.bel_code + k);
-        if (w & 1) {  // an enemy seat: the observer's combat-memory row of the piece
-            prefetch_l2(b.cm_direct_lo + k); prefetch_l2(b.cm_direct_hi + k); prefetch_l2(b.cm_chain_lo + k);
-            prefetch_l2(b.cm_chain_hi + k); prefetch_l2(b.cm_direct_type + k); prefetch_l2(b.cm_chain_type + k);
-            prefetch_l2(b.cm_direct_other + k); prefetch_l2(b.cm_rank_floor + k); prefetch_l2(b.cm_is_gongb + k);
-            prefetch_l2(b.cm_not_gongb + k); prefetch_l2(b.cm_atk_gongb + k);
-            prefetch_l2(b.cm_last_direct_step + k); prefetch_l2(b.cm_last_chain_step + k);
-            prefetch_l2(b.cm_rank_floor_step + k);
-        } else if (w == 0) {  // the observer's own pieces: the opponents' views and eaten-by sets
-            const size_t kl = OI(e, (o + 1) & 3, p), kr = OI(e, (o + 3) & 3, p);
-            prefetch_l2(b.cm_direct_lo + kl); prefetch_l2(b.cm_direct_hi + kl); prefetch_l2(b.cm_direct_other + kl);
-            prefetch_l2(b.cm_is_gongb + kl); prefetch_l2(b.cm_atk_gongb + kl);
-            prefetch_l2(b.cm_direct_lo + kr); prefetch_l2(b.cm_direct_hi + kr); prefetch_l2(b.cm_direct_other + kr);
-            prefetch_l2(b.cm_is_gongb + kr); prefetch_l2(b.cm_atk_gongb + kr);
-            prefetch_l2(b.cm_eaten_lo + k); prefetch_l2(b.cm_eaten_hi + k);
-        }
-    } else if (w == 0) {  // per-env rows
-        if (ln == 30) {
-            prefetch_l2(b.move_counter + e); prefetch_l2(b.mslc + e); prefetch_l2(b.hist_count + e);
-            prefetch_l2(b.seat_dead + (size_t)e * 4); prefetch_l2(b.seat_flag + (size_t)e * 4);
-        } else {
-            prefetch_l2(b.hist_src + (size_t)e * HIST); prefetch_l2(b.hist_dst + (size_t)e * HIST);
-            prefetch_l2(b.remaining + (size_t)e * 192 + o * 48);
-            prefetch_l2(b.remaining + (size_t)e * 192 + o * 48 + 47);
-        }
-    }
-}
-
 __device__ void stage_unit(const jq_batch &b, int seats, int mode, float *global, ObsSmem &S, UnitBuf &B, int u,
                            int o, int head, int t, int bar_stage) {
     const int e = u / seats;
@@ -540,31 +514,15 @@ __global__ void __launch_bounds__(OBS_THREADS, OBS_MIN_CTAS) obs_kernel(jq_batch
     extern __shared__ __align__(16) unsigned char smem_raw[];
     ObsSmem &S = *reinterpret_cast<ObsSmem *>(smem_raw);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    // once per CTA: plane kinds and the list of board-static bits (observation.py:343-383)
+    // once per CTA: observer rotations, belief tables and board-static words
+    // into shared memory; both bitstreams cleared
     for (int i = tid; i < 4 * NC; i += OBS_THREADS) (&S.rotf[0][0])[i] = (&g_topo.rotf[0][0])[i];
     for (int i = tid; i < 30 * 12; i += OBS_THREADS) S.prior[i] = g_prior[i];
     if (tid < 12) S.uniform[tid] = g_uniform[tid];
     if (tid < 30) S.slot_ch[tid] = g_topo.slot_ch[tid];
     for (int i = tid; i < 2 * OBS_WORDS4; i += OBS_THREADS)
         reinterpret_cast<uint4 *>(S.buf[i / OBS_WORDS4].bits)[i % OBS_WORDS4] = make_uint4(0u, 0u, 0u, 0u);
-    if (tid == 0) S.stat_n = 0;
-    __syncthreads();
-    for (int f = tid; f < NC; f += OBS_THREADS) {
-        const int cc = g_topo.f2c[f];
-        if (cc < 0) continue;
-        const uint8_t fl = g_topo.flags[cc];
-        const uint8_t fb[5] = {F_CAMP, F_SH, F_RAIL, F_NINE, F_ARC};
-#pragma unroll
-        for (int i = 0; i < 5; ++i)
-            if (fl & fb[i]) S.stat[atomicAdd(&S.stat_n, 1)] = (uint16_t)(i * NC + f);
-    }
-    for (int i = tid; i < 16 * STAT_WORDS; i += OBS_THREADS) (&S.statw[0][0][0])[i] = 0u;
-    __syncthreads();
-    for (int i = tid; i < 16 * S.stat_n; i += OBS_THREADS) {  // every (observer, offset, static bit)
-        const int os = i / S.stat_n, en = S.stat[i - os * S.stat_n], pl = en / NC, f = en - pl * NC;
-        const int q = (58 + pl) * NC + S.rotf[os >> 2][f] + (os & 3) + 1 - STAT_W0 * 32;
-        atomicOr(&S.statw[os >> 2][os & 3][q >> 5], 1u << (q & 31));
-    }
+    for (int i = tid; i < 16 * STAT_WORDS; i += OBS_THREADS) (&S.statw[0][0][0])[i] = (&g_statw[0][0][0])[i];
     __syncthreads();
     const int units = b.n * seats;
     if (warp < OBS_STREAM_WARPS) {
@@ -589,7 +547,6 @@ __global__ void __launch_bounds__(OBS_THREADS, OBS_MIN_CTAS) obs_kernel(jq_batch
         }
         bar_sync(BAR_STAGE, OBS_STAGE_THREADS);
         int u = S.ticket[0], o = S.next_o[0], u1 = S.ticket[1], o1 = S.next_o[1];
-        if (u1 < units) prefetch_unit(b, seats, u1, o1, t);
         int k = 0;
         for (;; ++k) {
             const int bi = k & 1;
@@ -612,7 +569,6 @@ __global__ void __launch_bounds__(OBS_THREADS, OBS_MIN_CTAS) obs_kernel(jq_batch
             o = o1;
             u1 = S.ticket[0];
             o1 = S.next_o[0];
-            if (u1 < units) prefetch_unit(b, seats, u1, o1, t);
             bar_arrive(BAR_FULL0 + bi, OBS_THREADS);
             bar_sync(BAR_STAGE, OBS_STAGE_THREADS);  // everyone has read the next ticket
         }
