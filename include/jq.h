@@ -284,6 +284,21 @@ int jq_csr_noalloc(int32_t n, const int32_t *d_counts, const int32_t *d_ids, int
 int jq_observe(const jq_batch *b, const int8_t *d_observers, int32_t seats_per_env,
                int32_t show_mode, float *d_spatial, float *d_global, void *stream);
 
+/* As jq_observe, with the belief input given by the caller instead of the
+ * library's own per-piece beliefs: d_beliefs is (N, 4, 12, 289) float32,
+ * [env][observer seat][tracked type][world flat cell] -- the reference's
+ * d_belief layout.  The observer's slice is written at each alive
+ * teammate / left / right piece's cell in channels 12-23 / 27-38 / 39-50
+ * where it is > 0, and global[0:12] / [12:24] are its float32 sums over the
+ * left / right enemy pieces' cells, added in ascending pid order (the
+ * reference adds them with atomics in no fixed order).  Everything else is
+ * jq_observe.  Replaces build_observation_batch with a beliefs argument
+ * (bindings.cpp:1091-1134; observation.cu:246-253, 330-370, 417-424,
+ * 533-544), e.g. beliefs refreshed by a belief network. */
+int jq_observe_beliefs(const jq_batch *b, const int8_t *d_observers, int32_t seats_per_env,
+                       int32_t show_mode, const float *d_beliefs, float *d_spatial, float *d_global,
+                       void *stream);
+
 /* Uniform-random legal action per env from jq_legal's output, counter-based
  * (seed, ply, env); -1 when an env has no legal action. */
 int jq_sample_uniform(int32_t n, const int32_t *d_counts, const int32_t *d_ids, int32_t cap,

@@ -84,6 +84,7 @@ SIGNATURES = {
     "jq_csr": (ctypes.c_int, [_i32, _vp, _vp, _i32, _vp, _vp, _vp, _vp]),
     "jq_csr_noalloc": (ctypes.c_int, [_i32, _vp, _vp, _i32, _vp, _vp, _vp]),
     "jq_observe": (ctypes.c_int, [_PB, _vp, _i32, _i32, _vp, _vp, _vp]),
+    "jq_observe_beliefs": (ctypes.c_int, [_PB, _vp, _i32, _i32, _vp, _vp, _vp, _vp]),
     "jq_sample_uniform": (ctypes.c_int, [_i32, _vp, _vp, _i32, _u64, _u64, _vp, _vp]),
     "jq_sample_softmax": (ctypes.c_int, [_PB, _vp, _vp, _i32, _u64, _u64, _vp, _vp, _vp]),
 }

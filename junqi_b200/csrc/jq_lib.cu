@@ -602,8 +602,8 @@ int jq_csr_noalloc(int32_t n, const int32_t *d_counts, const int32_t *d_ids, int
     return JQ_OK;
 }
 
-int jq_observe(const jq_batch *b, const int8_t *d_observers, int32_t seats_per_env, int32_t show_mode,
-               float *d_spatial, float *d_global, void *stream) {
+static int observe_launch(const jq_batch *b, const int8_t *d_observers, int32_t seats_per_env, int32_t show_mode,
+                          const float *d_beliefs, float *d_spatial, float *d_global, void *stream) {
     int rc = check_batch(b);
     if (rc) return rc;
     if (seats_per_env < 1 || seats_per_env > 4) return fail(JQ_ERR_ARG, "seats_per_env must be 1..4");
@@ -623,9 +623,20 @@ int jq_observe(const jq_batch *b, const int8_t *d_observers, int32_t seats_per_e
     if (grid > units) grid = units;
     int *ticket = st->obs_ticket + 2 * (st->obs_calls.fetch_add(1) % OBS_TICKETS);
     obs_kernel<<<(unsigned)grid, OBS_THREADS, obs_smem(), (cudaStream_t)stream>>>(
-        *b, d_observers, seats_per_env, show_mode, d_spatial, d_global, ticket);
+        *b, d_observers, seats_per_env, show_mode, d_spatial, d_global, ticket, d_beliefs);
     CU(cudaGetLastError());
     return JQ_OK;
+}
+
+int jq_observe(const jq_batch *b, const int8_t *d_observers, int32_t seats_per_env, int32_t show_mode,
+               float *d_spatial, float *d_global, void *stream) {
+    return observe_launch(b, d_observers, seats_per_env, show_mode, nullptr, d_spatial, d_global, stream);
+}
+
+int jq_observe_beliefs(const jq_batch *b, const int8_t *d_observers, int32_t seats_per_env, int32_t show_mode,
+                       const float *d_beliefs, float *d_spatial, float *d_global, void *stream) {
+    if (!d_beliefs || ((uintptr_t)d_beliefs & 3)) return fail(JQ_ERR_ARG, "beliefs must be a float32 array");
+    return observe_launch(b, d_observers, seats_per_env, show_mode, d_beliefs, d_spatial, d_global, stream);
 }
 
 int jq_sample_uniform(int32_t n, const int32_t *d_counts, const int32_t *d_ids, int32_t cap, uint64_t seed,

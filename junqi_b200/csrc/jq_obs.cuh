@@ -104,6 +104,7 @@ struct __align__(16) UnitBuf {
     int16_t pcell[NP];                  // canonical cell of an alive on-board piece, -1: none
     uint8_t pflag[NP];                  // bit 0: belief record, bit 1: combat-memory record
     uint8_t pbase[NP], pcode[NP];       // belief record: first plane (12 / 27 / 39) and belief code
+    float pbel[NP][12];                 // belief record with caller-given beliefs: the 12 values at the cell
     uint8_t bel_list[NP], cm_list[NP];  // pids holding a belief / combat-memory record
     int nbel, ncm;
     int32_t exc_pos[EXC_MAX];           // output float index of each exception
@@ -151,6 +152,7 @@ struct Stager {
     UnitBuf &B;
     int qoff;
     const int16_t *rotf;  // the observer's world -> canonical cell map
+    const float *ext;     // caller-given beliefs of this unit's observer, (12, 289) world frame; NULL: none
     __device__ __forceinline__ int q(int ch, int cell) const { return ch * NC + cell + qoff; }
     __device__ __forceinline__ void one(int ch, int cell) { set_bit(B.bits, q(ch, cell)); }
     __device__ __forceinline__ void exception(int j, float v) {
@@ -284,6 +286,14 @@ __device__ void stage_piece(const jq_batch &b, int e, int o, int mode, const Obs
             flag = 1;
             st.B.pbase[p] = (uint8_t)base;
             st.B.pcode[p] = (uint8_t)code;
+            if (st.ext) {
+                float v[12];
+                const float *src = st.ext + y * 17 + x;
+#pragma unroll
+                for (int t = 0; t < 12; ++t) v[t] = src[t * NC];
+#pragma unroll
+                for (int t = 0; t < 12; ++t) st.B.pbel[p][t] = v[t];
+            }
         }
         const int half = team == oteam ? 0 : 4;
         st.one(66 + half + (mcnt < 3 ? mcnt : 3), cell);
@@ -355,11 +365,12 @@ __device__ __forceinline__ int unit_observer(const jq_batch &b, const int8_t *ob
     return (observers ? observers[u] : (seats == 1 ? b.turn[e] : u % seats)) & 3;
 }
 
-__device__ void stage_unit(const jq_batch &b, int seats, int mode, float *global, ObsSmem &S, UnitBuf &B, int u,
-                           int o, int head, int t, int bar_stage) {
+__device__ void stage_unit(const jq_batch &b, int seats, int mode, const float *ext_bel, float *global, ObsSmem &S,
+                           UnitBuf &B, int u, int o, int head, int t, int bar_stage) {
     const int e = u / seats;
     const int tm = (o + 2) & 3, left = (o + 1) & 3, right = (o + 3) & 3;
-    Stager st{B, 4 - head, S.rotf[o]};  // B.bits arrive zeroed by the streaming warps
+    // B.bits arrive zeroed by the streaming warps
+    Stager st{B, 4 - head, S.rotf[o], ext_bel ? ext_bel + ((size_t)e * 4 + o) * 12 * NC : nullptr};
     if (t < 32) {  // observer-own pids per tracked type: one load per lane, one ballot per type
         const int ti = t < 30 ? tracked_idx(b.piece_type[PI(e, o * 30 + t)]) : -1;
         const int pos = o * 30;
@@ -374,7 +385,9 @@ __device__ void stage_unit(const jq_batch &b, int seats, int mode, float *global
     }
     if (t == 32) B.cval[0] = (float)fmin((double)b.mslc[e] / 200.0, 1.0);
     if (t == 33) B.cval[1] = (float)fmin((double)b.move_counter[e] / 4000.0, 1.0);
-    if (t >= 64 && t < 64 + OBS_GL) {  // globals (observation.py:1623-1651)
+    // globals (observation.py:1623-1651); with caller-given beliefs the
+    // streaming warps write global[0:24] from the belief records
+    if (t >= 64 + (ext_bel ? 24 : 0) && t < 64 + OBS_GL) {
         const int j = t - 64;
         float v;
         if (j < 24) {
@@ -448,8 +461,8 @@ __device__ void stage_unit(const jq_batch &b, int seats, int mode, float *global
 
 // Streaming warps: write unit B.u.  w = streaming warp 0..nwarps-1, t = its thread;
 // bar_stream is a named barrier of the nwarps streaming warps.
-__device__ void stream_unit(UnitBuf &B, const float *prior, const float *uniform, float *spatial, int w, int lane,
-                            int nwarps, int bar_stream) {
+__device__ void stream_unit(UnitBuf &B, const float *prior, const float *uniform, bool ext, float *spatial,
+                            float *global, int w, int lane, int nwarps, int bar_stream) {
     const int u = B.u, t = w * 32 + lane;
     float *out = spatial + (size_t)u * OBS_FLOATS;
     const int head = unit_head(spatial, u), qoff = 4 - head;
@@ -483,8 +496,19 @@ __device__ void stream_unit(UnitBuf &B, const float *prior, const float *uniform
     const int nb = B.nbel * 12, nc = B.ncm * 16;
     for (int i = t; i < nb; i += nthr) {
         const int j = i / 12, k = i - j * 12, p = B.bel_list[j];
-        const float v = bel_value(prior, uniform, B.pcode[p], k);
-        if (v != 0.f) out[(B.pbase[p] + k) * NC + B.pcell[p]] = v;
+        // caller-given beliefs are written where > 0 (observation.cu:330-370)
+        const float v = ext ? B.pbel[p][k] : bel_value(prior, uniform, B.pcode[p], k);
+        if (v > 0.f) out[(B.pbase[p] + k) * NC + B.pcell[p]] = v;
+    }
+    if (ext && t < 24) {
+        // global[0:24] from caller-given beliefs: their sums over the left /
+        // right enemy pieces' cells (observation.cu:417-424, 533-544), added
+        // in ascending pid order (the reference's float atomics have none)
+        const int base = t < 12 ? 27 : 39, k = t < 12 ? t : t - 12;
+        float acc = 0.f;
+        for (int p = 0; p < NP; ++p)
+            if (B.pcell[p] >= 0 && (B.pflag[p] & 1) && B.pbase[p] == base) acc += B.pbel[p][k];
+        global[(size_t)B.u * OBS_GL + t] = acc;
     }
     for (int i = t; i < nc; i += nthr) {
         const int j = i >> 4, k = i & 15, p = B.cm_list[j], cell = B.pcell[p];
@@ -510,7 +534,8 @@ __device__ void stream_unit(UnitBuf &B, const float *prior, const float *uniform
 // the next launch that uses this ticket.
 __global__ void __launch_bounds__(OBS_THREADS, OBS_MIN_CTAS) obs_kernel(jq_batch b, const int8_t *__restrict__ observers,
                                                                         int seats, int mode, float *spatial,
-                                                                        float *global, int *ticket) {
+                                                                        float *global, int *ticket,
+                                                                        const float *__restrict__ ext_bel) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     ObsSmem &S = *reinterpret_cast<ObsSmem *>(smem_raw);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -531,7 +556,8 @@ __global__ void __launch_bounds__(OBS_THREADS, OBS_MIN_CTAS) obs_kernel(jq_batch
             bar_sync(BAR_FULL0 + bi, OBS_THREADS);  // buffer bi staged
             UnitBuf &B = S.buf[bi];
             if (B.u < 0) break;
-            stream_unit(B, S.prior, S.uniform, spatial, warp, lane, OBS_STREAM_WARPS, BAR_STREAM);
+            stream_unit(B, S.prior, S.uniform, ext_bel != nullptr, spatial, global, warp, lane, OBS_STREAM_WARPS,
+                        BAR_STREAM);
             bar_arrive(BAR_EMPTY0 + bi, OBS_THREADS);  // buffer bi free again
         }
     } else {
@@ -562,7 +588,7 @@ __global__ void __launch_bounds__(OBS_THREADS, OBS_MIN_CTAS) obs_kernel(jq_batch
                 un = atomicAdd(&ticket[0], 1);
                 on = un < units ? unit_observer(b, observers, seats, un) : 0;
             }
-            stage_unit(b, seats, mode, global, S, B, u, o, unit_head(spatial, u), t, BAR_STAGE);
+            stage_unit(b, seats, mode, ext_bel, global, S, B, u, o, unit_head(spatial, u), t, BAR_STAGE);
             if (t == 0) { S.ticket[0] = un; S.next_o[0] = on; }
             bar_sync(BAR_STAGE, OBS_STAGE_THREADS);  // unit staged; the ticket after next published
             u = u1;

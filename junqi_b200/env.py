@@ -160,14 +160,26 @@ class JunqiEnvB200:
                                _stream_ptr()), "jq_csr")
         return self.offsets, self.values
 
-    def observe(self, observers: torch.Tensor | None = None, seats_per_env: int | None = None):
+    def observe(self, observers: torch.Tensor | None = None, seats_per_env: int | None = None,
+                beliefs: torch.Tensor | None = None):
+        """Observations of `observers` (default: each env's turn, or seats 0..3).  With `beliefs`
+        ((N, 4, 12, 289) float32 per-cell beliefs, e.g. a belief network's output) the belief
+        planes and global[0:24] come from them instead of the env's own beliefs."""
         s = self.obs_seats if seats_per_env is None else int(seats_per_env)
         if self.spatial is None or self.spatial.shape[0] < self.n * s:
             self.spatial = torch.empty((self.n * s, OBS_CHANNELS, 17, 17), dtype=torch.float32, device=self.device)
             self.global_ = torch.empty((self.n * s, OBS_GLOBAL), dtype=torch.float32, device=self.device)
         o = None if observers is None else observers.to(device=self.device, dtype=torch.int8).contiguous()
-        N.check(N.lib().jq_observe(ctypes.byref(self.batch.struct), self._ptr(o), s, self.show_mode,
-                                   self.spatial.data_ptr(), self.global_.data_ptr(), _stream_ptr()), "jq_observe")
+        if beliefs is None:
+            N.check(N.lib().jq_observe(ctypes.byref(self.batch.struct), self._ptr(o), s, self.show_mode,
+                                       self.spatial.data_ptr(), self.global_.data_ptr(), _stream_ptr()), "jq_observe")
+        else:
+            bel = beliefs.to(device=self.device, dtype=torch.float32).contiguous()
+            if tuple(bel.shape) != (self.n, 4, 12, 289):
+                raise ValueError(f"beliefs must be ({self.n}, 4, 12, 289), got {tuple(bel.shape)}")
+            N.check(N.lib().jq_observe_beliefs(ctypes.byref(self.batch.struct), self._ptr(o), s, self.show_mode,
+                                               bel.data_ptr(), self.spatial.data_ptr(), self.global_.data_ptr(),
+                                               _stream_ptr()), "jq_observe_beliefs")
         return self.spatial[: self.n * s], self.global_[: self.n * s]
 
     def sample_uniform(self, seed: int, ply: int) -> torch.Tensor:

@@ -7,9 +7,13 @@ the sm_100a kernels of ``libjq.so``.  Differences a caller can observe:
 * Beliefs are part of the device state and follow ``BeliefTensor`` exactly
   (info_model.py), updated inside the step.  ``update_beliefs_after_step``,
   ``record_move_history``, ``snapshot_pre_step_flags`` and
-  ``init_beliefs_for_reset_envs`` are therefore no-ops, and the per-cell
-  float beliefs accepted by ``upload_beliefs`` / ``build_observation_batch``
-  are validated but not needed.
+  ``init_beliefs_for_reset_envs`` are therefore no-ops.
+* Per-cell float beliefs given to ``upload_beliefs`` /
+  ``build_observation_batch`` (e.g. a belief network's output) are used as
+  given by every observation built afterwards (``jq_observe_beliefs``) until
+  ``init_all_beliefs`` or ``gpu_scratch_reset``; steps do not apply the
+  reference's per-cell float update rules to them (belief.cu:255-568), and
+  ``DeviceRolloutHistory`` records the library's own beliefs.
 * Resets reproduce ``GameState.new_game`` exactly (full initial Zobrist
   hash, -1 in unused slots); the pool entry is ``jq_pool_index(seed, k, env)``
   where k counts reset calls.
@@ -128,15 +132,20 @@ def upload_seat_strongholds(strongholds) -> None:
         raise RuntimeError("upload_seat_strongholds: expected 8 entries")
 
 
-_beliefs_uploaded = False
+_beliefs: torch.Tensor | None = None  # uploaded per-cell beliefs (N, 4, 12, 289) float32
 _observer_seats: torch.Tensor | None = None
 
 
 def upload_beliefs(num_envs: int, beliefs) -> None:
-    global _beliefs_uploaded
-    if np.asarray(beliefs).size != num_envs * 4 * 12 * 289:
+    """bindings.cpp:1136-1149: per-cell beliefs [env][observer][type][world cell]."""
+    global _beliefs
+    if torch.is_tensor(beliefs):
+        t = beliefs.detach().to(device=f"cuda:{_device}", dtype=torch.float32)
+    else:
+        t = torch.from_numpy(np.ascontiguousarray(beliefs, dtype=np.float32)).to(f"cuda:{_device}")
+    if t.numel() != num_envs * 4 * 12 * 289:
         raise RuntimeError("beliefs: expected (N, 4, 12, 289) float32")
-    _beliefs_uploaded = True
+    _beliefs = t.reshape(num_envs, 4, 12, 289).contiguous()
 
 
 def upload_observer_seats(num_envs: int, observer_seats) -> None:
@@ -148,7 +157,10 @@ def upload_observer_seats(num_envs: int, observer_seats) -> None:
 
 
 def gpu_scratch_reset() -> None:
-    pass
+    """Forget uploaded beliefs and observer seats."""
+    global _beliefs, _observer_seats
+    _beliefs = None
+    _observer_seats = None
 
 
 def device_synchronize() -> None:
@@ -407,6 +419,9 @@ def init_beliefs_for_reset_envs(state) -> None:
 
 
 def init_all_beliefs(state: DeviceGameStateBatch) -> None:
+    """Prior beliefs for every env; observations use the library's beliefs again."""
+    global _beliefs
+    _beliefs = None
     N.check(N.lib().jq_init_beliefs(ctypes.byref(state.b.struct), state.show_mode, _stream()), "jq_init_beliefs")
 
 
@@ -420,12 +435,19 @@ def reset_terminated_envs(state: DeviceGameStateBatch, seed: int) -> None:
 
 
 def _observe(state, observers_ptr, seats, show_mode, sp_ptr, gl_ptr):
-    N.check(N.lib().jq_observe(ctypes.byref(state.b.struct), observers_ptr, seats, int(show_mode), sp_ptr, gl_ptr,
-                               _stream()), "jq_observe")
+    if _beliefs is None:
+        N.check(N.lib().jq_observe(ctypes.byref(state.b.struct), observers_ptr, seats, int(show_mode), sp_ptr,
+                                   gl_ptr, _stream()), "jq_observe")
+        return
+    if _beliefs.shape[0] != state.num_envs:
+        raise RuntimeError(f"uploaded beliefs are for {_beliefs.shape[0]} envs, the state has {state.num_envs}; "
+                           "upload matching beliefs or call init_all_beliefs / gpu_scratch_reset")
+    N.check(N.lib().jq_observe_beliefs(ctypes.byref(state.b.struct), observers_ptr, seats, int(show_mode),
+                                       _beliefs.data_ptr(), sp_ptr, gl_ptr, _stream()), "jq_observe_beliefs")
 
 
 def build_observation_batch(state, beliefs, observer_seats, obs_out: DeviceObservationBatch, show_mode=2) -> None:
-    """bindings.cpp:1091-1134; per-cell float beliefs are not used (see module doc)."""
+    """bindings.cpp:1091-1134: observations of the given observers from the given per-cell beliefs."""
     upload_beliefs(state.num_envs, beliefs)
     upload_observer_seats(state.num_envs, observer_seats)
     _observe(state, _observer_seats.data_ptr(), 4, show_mode, obs_out.d_spatial_ptr, obs_out.d_global_ptr)

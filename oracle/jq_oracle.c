@@ -1474,6 +1474,52 @@ int jqo_init_beliefs(jqo_batch *b, int e, int mode) {
     return 0;
 }
 
+/* Observation with caller-given per-cell float beliefs, restating the
+ * reference GPU encoder's belief input (src/env/cuda/src/observation.cu):
+ * the observer's (12, 289) slice of bel (246-253) is written at each alive
+ * teammate / left / right piece's cell, in channels 12-23 / 27-38 / 39-50,
+ * where it is > 0 (330-370); global[0:12] and [12:24] are its sums over the
+ * left and right enemy pieces' cells (417-424, 533-544).  The reference adds
+ * those per-piece values with float atomics in no fixed order; here they are
+ * added in ascending pid order.  Everything else is jqo_obs.  bel is this
+ * env's (4, 12, 289) float32 block: [observer][type][world flat]. */
+int jqo_obs_ext(const jqo_batch *b, int e, int o, int mode, const float *bel, float *sp, float *gl) {
+    jqo_obs(b, e, o, mode, sp, gl);
+    const int *rot = T_rot[o];
+    const float *bo = bel + (size_t)o * 12 * NC;
+    const int tm = (o + 2) % 4, left = (o + 1) % 4, right = (o + 3) % 4;
+    float rl[12], rr[12];
+    for (int t = 0; t < 12; ++t) rl[t] = rr[t] = 0.f;
+    for (int p = 0; p < NP; ++p) {
+        size_t q = PI(e, p);
+        if (!b->alive[q]) continue;
+        const int f = b->pos_y[q] * 17 + b->pos_x[q], s = b->piece_seat[q];
+        const int base = s == tm ? 12 : s == left ? 27 : s == right ? 39 : -1;
+        if (base < 0) continue;
+        for (int t = 0; t < 12; ++t) {
+            const float x = bo[(size_t)t * NC + f];
+            sp[(size_t)(base + t) * NC + rot[f]] = x > 0.f ? x : 0.f;
+            if (s == left) rl[t] += x;
+            if (s == right) rr[t] += x;
+        }
+    }
+    for (int t = 0; t < 12; ++t) {
+        gl[t] = rl[t];
+        gl[12 + t] = rr[t];
+    }
+    return 0;
+}
+
+int jqo_obs_ext_batch(const jqo_batch *b, const int8_t *observers, int mode, const float *bel, float *sp,
+                      float *gl, int nthreads) {
+    build_topology();
+#pragma omp parallel for schedule(dynamic, 8) num_threads(nthreads > 0 ? nthreads : 1)
+    for (int e = 0; e < b->n; ++e)
+        jqo_obs_ext(b, e, observers[e], mode, bel + (size_t)e * 4 * 12 * NC, sp + (size_t)e * JQO_OBS_CH * NC,
+                    gl + (size_t)e * JQO_OBS_GLOBAL);
+    return 0;
+}
+
 int jqo_obs_batch(const jqo_batch *b, const int8_t *observers, int mode, float *sp, float *gl,
                   int nthreads) {
     build_topology();

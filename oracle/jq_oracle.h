@@ -112,6 +112,12 @@ int jqo_obs(const jqo_batch *b, int env, int observer, int show_mode, float *spa
             float *global);
 int jqo_obs_batch(const jqo_batch *b, const int8_t *observers, int show_mode,
                   float *spatial, float *global, int nthreads);
+/* As jqo_obs / jqo_obs_batch, with caller-given per-cell float beliefs
+ * bel (N, 4, 12, 289) in the belief planes and global[0:24]. */
+int jqo_obs_ext(const jqo_batch *b, int env, int observer, int show_mode, const float *bel, float *spatial,
+                float *global);
+int jqo_obs_ext_batch(const jqo_batch *b, const int8_t *observers, int show_mode, const float *bel,
+                      float *spatial, float *global, int nthreads);
 #ifdef __cplusplus
 }
 #endif

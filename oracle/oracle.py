@@ -322,6 +322,21 @@ class OracleBatch:
                             _ptr(sp, ctypes.c_float), _ptr(gl, ctypes.c_float), self.threads)
         return sp, gl
 
+    def obs_beliefs(self, beliefs: np.ndarray, observers: np.ndarray | None = None):
+        """As ``obs`` with caller-given float beliefs (N, 4, 12, 289) [env,
+        observer, type, world cell]: the reference GPU encoder's belief
+        input (observation.cu:246-253, 330-370, 417-424, 533-544); the
+        enemy sums of global[0:24] are added in ascending pid order."""
+        obsv = self.a["turn"] if observers is None else np.ascontiguousarray(observers, dtype=np.int8)
+        bel = np.ascontiguousarray(beliefs, dtype=np.float32)
+        assert bel.shape == (self.n, 4, 12, 289)
+        sp = np.zeros((self.n, OBS_CH, 17, 17), np.float32)
+        gl = np.zeros((self.n, OBS_GL), np.float32)
+        lib().jqo_obs_ext_batch(ctypes.byref(self._c), _ptr(obsv, ctypes.c_int8), self.show_mode,
+                                _ptr(bel, ctypes.c_float), _ptr(sp, ctypes.c_float), _ptr(gl, ctypes.c_float),
+                                self.threads)
+        return sp, gl
+
     def obs_one(self, env: int, observer: int):
         sp = np.zeros((OBS_CH, 17, 17), np.float32)
         gl = np.zeros(OBS_GL, np.float32)

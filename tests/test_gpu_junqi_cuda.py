@@ -31,6 +31,7 @@ REF_KEYS = {"piece_seat_arr": "piece_seat", "piece_type_arr": "piece_type", "ali
 def _setup():
     jc.set_device(0)
     jc.init_tables()
+    jc.gpu_scratch_reset()
     z = tables.zobrist_tables()
     jc.upload_zobrist_tables(z["piece"].ravel(), z["turn"], z["move_counter"], z["mslc"], z["winner"],
                              int(z["terminated"][0]), int(z["draw"][0]), z["seat_dead"], z["seat_flag"])
@@ -103,13 +104,23 @@ def test_reset_pool_and_single_seat_observation_match_oracle():
     sp, gl = obs.copy_to_host()
     osp, ogl = orc.obs()
     assert np.array_equal(sp, osp) and np.array_equal(gl, ogl)
+    # build_observation_batch with per-cell beliefs (a belief network's output, say)
+    bel = np.random.default_rng(3).random((n, 4, 12, 289)).astype(np.float32)
+    bel[bel < 0.3] = 0.0
     obs4 = jc.DeviceObservationBatch(n)
-    jc.build_observation_batch(state, np.zeros((n, 4, 12, 289), np.float32),
-                               np.tile(np.arange(4, dtype=np.int8), (n, 1)), obs4, 2)
-    sp4, _ = obs4.copy_to_host()
+    jc.build_observation_batch(state, bel, np.tile(np.arange(4, dtype=np.int8), (n, 1)), obs4, 2)
+    sp4, gl4 = obs4.copy_to_host()
     for s in range(4):
-        o_sp, _ = orc.obs(np.full(n, s, np.int8))
-        assert np.array_equal(sp4[:, s], o_sp)
+        o_sp, o_gl = orc.obs_beliefs(bel, np.full(n, s, np.int8))
+        assert np.array_equal(sp4[:, s], o_sp) and np.array_equal(gl4[:, s], o_gl)
+    # the uploaded beliefs stay in use (resident / single-seat builds) until init_all_beliefs
+    jc.build_observation_single_seat(state, obs, seats.data_ptr(), 2)
+    sp1, gl1 = obs.copy_to_host()
+    o_sp, o_gl = orc.obs_beliefs(bel)
+    assert np.array_equal(sp1, o_sp) and np.array_equal(gl1, o_gl)
+    jc.init_all_beliefs(state)
+    jc.build_observation_single_seat(state, obs, seats.data_ptr(), 2)
+    assert np.array_equal(obs.copy_to_host()[0], osp)
 
 
 def test_step_device_pointer_dict():

@@ -239,3 +239,38 @@ def test_slot_mask_matches_oracle(late):
                     e, p, s = np.argwhere(got != exp)[0]
                     raise AssertionError(f"ply {t}: slot mask differs at env {e} pid {p} slot {s}")
         env.ply(env.sample_uniform(seed, t), seed=seed, ply=t)
+
+
+@pytest.mark.parametrize("mode", [0, 1, 2])
+def test_observe_with_caller_beliefs_matches_oracle(mode):
+    """jq_observe_beliefs: per-cell float beliefs (zeros, one-hots, random,
+    negatives and NaNs, which the reference GPU encoder writes as 0) against
+    the oracle, mid-game, for the acting seat and for all four seats."""
+    n = 96
+    env = JunqiEnvB200(n, show_mode=mode, pool=tables.build_setup_pool(64, seed=9), rules=N.RULES_GAMESTATE)
+    env.reset(seed=4)
+    for t in range(1, 70):
+        env.ply(env.sample_uniform(4, t), seed=4, ply=t)
+    rng = np.random.default_rng(mode)
+    bel = rng.random((n, 4, 12, 289)).astype(np.float32)
+    bel[bel < 0.25] = 0.0
+    bel[rng.random(bel.shape) < 0.02] = -0.5
+    bel[rng.random(bel.shape) < 0.01] = np.nan
+    bel[:, :, 3] = 1.0
+    orc = O.OracleBatch(n, mode, rules=1)
+    O.load_state(orc, env.state(), init_beliefs=False)
+    dbel = torch.from_numpy(bel).cuda()
+    sp, gl = env.observe(None, seats_per_env=1, beliefs=dbel)
+    o_sp, o_gl = orc.obs_beliefs(bel)
+    assert np.array_equal(sp.cpu().numpy().view(np.int32), o_sp.view(np.int32))
+    # a NaN belief makes its enemy sum NaN; NaN payloads differ between CPU and GPU adds
+    assert np.array_equal(gl.cpu().numpy(), o_gl, equal_nan=True)
+    sp4, gl4 = env.observe(None, seats_per_env=4, beliefs=dbel)
+    sp4, gl4 = sp4.cpu().numpy().reshape(n, 4, 317, 17, 17), gl4.cpu().numpy().reshape(n, 4, 28)
+    for s in range(4):
+        o_sp, o_gl = orc.obs_beliefs(bel, np.full(n, s, np.int8))
+        assert np.array_equal(sp4[:, s], o_sp) and np.array_equal(gl4[:, s], o_gl, equal_nan=True), s
+    # the env's own beliefs are untouched
+    sp0, gl0 = env.observe(None, seats_per_env=1)
+    o_sp0, o_gl0 = orc.obs()
+    assert np.array_equal(sp0.cpu().numpy(), o_sp0) and np.array_equal(gl0.cpu().numpy(), o_gl0)
