@@ -239,6 +239,28 @@ static int check_batch(const jq_batch *b) {
 static size_t rule_smem() { return sizeof(RuleSmem); }
 static size_t obs_smem() { return sizeof(ObsSmem); }
 
+// Programmatic dependent launch: the kernel may be scheduled while the
+// previous kernel in the stream drains (the rules kernel's slowest envs, the
+// observation kernel's last units), load its board tables into shared
+// memory, then wait (griddepcontrol.wait) for that kernel to complete
+// before touching any state.  Kernels launched this way call
+// griddepcontrol.wait before their first access to caller memory.
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pdl(void (*kernel)(KArgs...), unsigned grid, unsigned block, size_t smem, cudaStream_t s,
+                              Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(block);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 static int launch_rules(RuleArgs &a, cudaStream_t s) {
     DeviceState *st;
     int rc = current_dev(st);
@@ -247,8 +269,7 @@ static int launch_rules(RuleArgs &a, cudaStream_t s) {
     int blocks = (a.b.n + RULE_WARPS - 1) / RULE_WARPS;
     int cap_blocks = st->sms * (st->rule_blocks_per_sm > 0 ? st->rule_blocks_per_sm : 1) * 4;
     if (blocks > cap_blocks) blocks = cap_blocks;
-    rules_kernel<<<blocks, RULE_THREADS, rule_smem(), s>>>(a);
-    CU(cudaGetLastError());
+    CU(launch_pdl(rules_kernel, (unsigned)blocks, RULE_THREADS, rule_smem(), s, a));
     return JQ_OK;
 }
 
@@ -622,9 +643,8 @@ static int observe_launch(const jq_batch *b, const int8_t *d_observers, int32_t 
     size_t grid = (size_t)st->sms * (st->obs_blocks_per_sm > 0 ? st->obs_blocks_per_sm : 1);
     if (grid > units) grid = units;
     int *ticket = st->obs_ticket + 2 * (st->obs_calls.fetch_add(1) % OBS_TICKETS);
-    obs_kernel<<<(unsigned)grid, OBS_THREADS, obs_smem(), (cudaStream_t)stream>>>(
-        *b, d_observers, seats_per_env, show_mode, d_spatial, d_global, ticket, d_beliefs);
-    CU(cudaGetLastError());
+    CU(launch_pdl(obs_kernel, (unsigned)grid, OBS_THREADS, obs_smem(), (cudaStream_t)stream, *b, d_observers,
+                  (int)seats_per_env, (int)show_mode, d_spatial, d_global, ticket, d_beliefs));
     return JQ_OK;
 }
 

@@ -539,6 +539,7 @@ __global__ void __launch_bounds__(OBS_THREADS, OBS_MIN_CTAS) obs_kernel(jq_batch
     extern __shared__ __align__(16) unsigned char smem_raw[];
     ObsSmem &S = *reinterpret_cast<ObsSmem *>(smem_raw);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    asm volatile("griddepcontrol.launch_dependents;");
     // once per CTA: observer rotations, belief tables and board-static words
     // into shared memory; both bitstreams cleared
     for (int i = tid; i < 4 * NC; i += OBS_THREADS) (&S.rotf[0][0])[i] = (&g_topo.rotf[0][0])[i];
@@ -548,6 +549,9 @@ __global__ void __launch_bounds__(OBS_THREADS, OBS_MIN_CTAS) obs_kernel(jq_batch
     for (int i = tid; i < 2 * OBS_WORDS4; i += OBS_THREADS)
         reinterpret_cast<uint4 *>(S.buf[i / OBS_WORDS4].bits)[i % OBS_WORDS4] = make_uint4(0u, 0u, 0u, 0u);
     for (int i = tid; i < 16 * STAT_WORDS; i += OBS_THREADS) (&S.statw[0][0][0])[i] = (&g_statw[0][0][0])[i];
+    // launched as a programmatic dependent (see the rules kernel): caller
+    // memory -- tickets, state, outputs -- only after the previous kernel
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     __syncthreads();
     const int units = b.n * seats;
     if (warp < OBS_STREAM_WARPS) {

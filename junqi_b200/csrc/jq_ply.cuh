@@ -87,8 +87,13 @@ __device__ bool warp_ply_env(const RuleArgs &a, const Topo &T, WEnv &w, int e, i
 __global__ void __launch_bounds__(RULE_THREADS, 4) rules_kernel(RuleArgs a) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     RuleSmem &S = *reinterpret_cast<RuleSmem *>(smem_raw);
+    // launched as a programmatic dependent: the next kernel may start its
+    // own table loads now; state is touched only after the previous kernel
+    // in the stream has completed
+    asm volatile("griddepcontrol.launch_dependents;");
     stage_topo(S.topo, threadIdx.x, RULE_THREADS);
     if (threadIdx.x == 0) S.applied = 0;
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     WEnv &w = S.w[warp];
