@@ -1,0 +1,123 @@
+"""Edge cases of the device path against the oracle.
+
+* Batches that fill no CTA evenly (1 and 13 envs) roll out bit-exactly,
+  through terminations and auto-resets from late-game starts.
+* A legal-id capacity below the move count keeps the full count, the first
+  `cap` ids and a complete canonical mask; the CSR holds min(count, cap).
+* Terminated envs and envs whose acting seat is dead have no legal moves
+  and an all-zero mask row (batched_state.py:394-399).
+* Invalid actions (none, out of range, from an empty cell, in a finished
+  game) leave the env untouched and report valid = 0.
+* Explicit observer lists of any order give the oracle's observation of
+  each listed seat.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from junqi_b200 import _native as N
+from junqi_b200 import tables
+from junqi_b200.env import HALF_DARK, JunqiEnvB200
+from junqi_b200.workloads import late_game_starts
+from oracle import oracle as O
+from tests.test_gpu_parity import _compare_legal, _compare_obs, _compare_state
+
+pytestmark = pytest.mark.gpu
+
+
+def _pair(n, seed, rules=N.RULES_GAMESTATE, late=False, **kw):
+    pool = tables.build_setup_pool(64, seed=seed)
+    env = JunqiEnvB200(n, pool=pool, rules=rules, **kw)
+    env.reset(seed=seed)
+    if late:
+        late_game_starts(env, seed)
+    orc = O.OracleBatch(n, env.show_mode, rules=rules)
+    O.load_state(orc, env.state(), init_beliefs=False)
+    return env, orc, pool
+
+
+@pytest.mark.parametrize("n", [1, 13])
+def test_ragged_batches_roll_out_bit_exactly(n):
+    env, orc, pool = _pair(n, 21, late=True)
+    L = N.lib()
+    ends = 0
+    for t in range(1, 401):
+        acts = env.sample_uniform(21, t)
+        a = acts.cpu().numpy().copy()
+        out = env.ply(acts, seed=21, ply=t)
+        r = orc.step(a)
+        for k in ("valid", "event", "terminated", "winner", "draw", "reward"):
+            assert np.array_equal(out[k].cpu().numpy().astype(r[k].dtype), r[k]), (t, k)
+        for e in np.nonzero(r["terminated"])[0]:
+            orc.reset_env(int(e), pool[L.jq_pool_index(21, t, int(e), pool.shape[0])])
+            ends += 1
+        _compare_state(env, orc, t)
+        _compare_legal(env, orc, t, masks=(t % 25 == 0))
+        if t % 100 == 0:
+            _compare_obs(env, orc, t, seats=1)
+    assert ends >= 1
+
+
+def test_small_legal_capacity_truncates_ids_not_counts():
+    env, orc, _ = _pair(32, 5, legal_cap=4)
+    for t in range(1, 30):
+        env.ply(env.sample_uniform(5, t), seed=5, ply=t)
+    O.load_state(orc, env.state(), init_beliefs=False)
+    o_off, o_val = orc.legal()
+    counts = env.counts.cpu().numpy()
+    ids = env.ids.cpu().numpy()
+    assert np.array_equal(counts, np.diff(o_off)) and (counts > 4).any()
+    for e in range(32):
+        k = min(int(counts[e]), 4)
+        assert np.array_equal(ids[e, :k], o_val[o_off[e]:o_off[e] + k])
+        exp = orc.canonical_mask(o_val[o_off[e]:o_off[e + 1]], int(orc["turn"][e]))
+        assert np.array_equal(env.mask[e].cpu().numpy().astype(bool), exp)
+    off, val = env.csr()
+    assert np.array_equal(np.diff(off.cpu().numpy()), np.minimum(counts, 4))
+
+
+def test_finished_games_and_dead_seats_have_no_moves():
+    env, orc, _ = _pair(8, 9)
+    st = env.state()
+    st["terminated"][:3] = 1
+    turn = st["turn"].astype(np.int64)
+    st["seat_dead"].reshape(8, 4)[3:6, :] = 0
+    for e in range(3, 6):
+        st["seat_dead"].reshape(8, 4)[e, turn[e]] = 1
+    env.batch.load({"terminated": st["terminated"], "seat_dead": st["seat_dead"]})
+    env.mask.fill_(1)
+    counts, _ = env.legal()
+    c = counts.cpu().numpy()
+    assert (c[:6] == 0).all() and (c[6:] > 0).all()
+    assert not env.mask[:6].any() and env.mask[6:].any()
+
+
+def test_invalid_actions_leave_the_env_untouched():
+    env, orc, _ = _pair(6, 3)
+    st = env.state()
+    st["terminated"][5] = 1
+    env.batch.load({"terminated": st["terminated"]})
+    before = env.state()
+    empty_src = int(np.nonzero(before["cell_pid"][2] < 0)[0][0])
+    acts = torch.tensor([-1, 289 * 289, empty_src * 289 + 10, 16641 * 5 + 7, -7, 0], dtype=torch.int32)
+    out = env.step(acts.cuda())
+    assert not out["valid"].any()
+    after = env.state()
+    for k in ("zobrist", "cell_pid", "turn", "move_counter", "alive", "pos_x", "pos_y"):
+        assert np.array_equal(before[k], after[k]), k
+
+
+def test_explicit_observer_lists():
+    env, orc, _ = _pair(10, 4)
+    for t in range(1, 25):
+        env.ply(env.sample_uniform(4, t), seed=4, ply=t)
+    O.load_state(orc, env.state(), init_beliefs=False)
+    rng = np.random.default_rng(0)
+    obs = np.stack([rng.permutation(4)[:3] for _ in range(10)]).astype(np.int8)  # 3 seats per env, any order
+    sp, gl = env.observe(torch.from_numpy(obs).cuda(), seats_per_env=3)
+    sp, gl = sp.cpu().numpy().reshape(10, 3, 317, 17, 17), gl.cpu().numpy().reshape(10, 3, 28)
+    for j in range(3):
+        o_sp, o_gl = orc.obs(obs[:, j].copy())
+        assert np.array_equal(sp[:, j], o_sp) and np.array_equal(gl[:, j], o_gl), j
