@@ -396,7 +396,7 @@ def run_e2e(env, args, seed, stream) -> dict:
     # while the observation kernel (consumed on the device by the policy) keeps
     # running on the main stream.
     copy_stream = torch.cuda.Stream(device=env.device)
-    csr_done = torch.cuda.Event()
+    csr_done, acts_up = torch.cuda.Event(), torch.cuda.Event()
     torch.cuda.synchronize()
     import torch.distributed as dist
     if dist.is_initialized():
@@ -408,8 +408,11 @@ def run_e2e(env, args, seed, stream) -> dict:
         pick = (rng.random(n) * np.maximum(cnt, 1)).astype(np.int64)
         v = val_h.numpy()
         acts_h.numpy()[:] = np.where(cnt > 0, v[np.minimum(o[:-1] + pick, max(int(o[-1]) - 1, 0))], -1)
-        acts_d.copy_(acts_h, non_blocking=True)
+        with torch.cuda.stream(copy_stream):  # upload under the observation kernel still running
+            acts_d.copy_(acts_h, non_blocking=True)
+            acts_up.record(copy_stream)
         h2d += n * 4
+        stream.wait_event(acts_up)
         env.ply(acts_d, seed=seed, ply=100_000 + t)
         off, val = env.csr()
         csr_done.record(stream)
@@ -434,8 +437,8 @@ def run_e2e(env, args, seed, stream) -> dict:
     applied = sharding.sum_over_ranks(applied, env.device)
     return {"value": applied / (ms / 1e3), "unit": "plies/s", "h2d_bytes_per_step": h2d // steps,
             "d2h_bytes_per_step": d2h // steps, "steps": steps,
-            "api": "JunqiEnvB200.ply/csr/observe with pinned host actions in, MoveResult + CSR out (side-stream "
-                   "copies overlap the observation kernel)"}
+            "api": "JunqiEnvB200.ply/csr/observe with pinned host actions in, MoveResult + CSR out (upload and "
+                   "copies on a side stream overlap the observation kernel)"}
 
 
 if __name__ == "__main__":
