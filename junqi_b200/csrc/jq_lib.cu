@@ -325,6 +325,11 @@ int jq_init(int device) {
     CU(cudaMemcpyToSymbol(g_topo, &host_topo, sizeof(Topo)));
     CU(cudaMemcpyToSymbol(g_slot, &host_slot, sizeof(SlotTopo)));
     {
+        static uint32_t rays[NB][4][NW];
+        if (!build_ray_masks(host_topo, rays)) return fail(JQ_ERR_ARG, "straight rail rays out of order");
+        CU(cudaMemcpyToSymbol(g_ray, rays, sizeof(rays)));
+    }
+    {
         static uint32_t statw[4][4][STAT_WORDS];
         build_static_words(host_topo, statw);
         CU(cudaMemcpyToSymbol(g_statw, statw, sizeof(statw)));

@@ -34,6 +34,7 @@ __constant__ int64_t c_zterm, c_zdraw;
 __device__ int64_t g_zpiece[NP * 14 * NC];
 __device__ int64_t g_zmc[4096];
 __device__ int64_t g_zmslc[512];
+__device__ uint32_t g_ray[NB][4][NW];  // straight rail rays as cell masks (build_ray_masks)
 __device__ float g_prior[30 * 12];
 __device__ float g_uniform[12];
 __device__ float g_recency[4 * RECENCY_LEN];
@@ -197,13 +198,30 @@ __device__ void piece_dsts(const Topo &T, int c, int t, const uint32_t (&empty)[
 #pragma unroll
         for (int i = 0; i < NW; ++i) out[i] |= landing[i];
     } else {
-        for (int k = 0; k < 4; ++k)
-            for (int l = 0; l < 12; ++l) {
-                int nb = T.sray[c][k][l];
-                if (nb == NONE8) break;
-                if (rbit(land, nb)) rset(out, nb);
-                if (!rbit(empty, nb)) break;
+        // straight rays as masks: the cells up to and including the first
+        // occupied one (the nearest blocker is the lowest set bit on rays of
+        // increasing index, the highest on the others), then those a piece
+        // may land on -- the same set as walking the ray cell by cell
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            uint32_t r[NW];
+#pragma unroll
+            for (int i = 0; i < NW; ++i) r[i] = __ldg(&g_ray[c][k][i]);
+            int stop = (k & 1) ? -1 : (1 << 20);  // no blocker: the whole ray
+#pragma unroll
+            for (int i = 0; i < NW; ++i) {
+                const int ii = (k & 1) ? i : NW - 1 - i;  // the nearest blocker is seen last
+                const uint32_t bl = r[ii] & ~empty[ii];
+                if (bl) stop = (k & 1) ? ii * 32 + 31 - __clz(bl) : ii * 32 + __ffs(bl) - 1;
             }
+#pragma unroll
+            for (int i = 0; i < NW; ++i) {
+                const int lim = stop - i * 32;
+                const uint32_t keep = (k & 1) ? (lim <= 0 ? ~0u : (lim > 31 ? 0u : ~((1u << lim) - 1u)))
+                                              : (lim < 0 ? 0u : (lim >= 31 ? ~0u : (2u << lim) - 1u));
+                out[i] |= r[i] & keep & land[i];
+            }
+        }
         if (T.flags[c] & F_CURVE_ACTIVE)
             for (int k = 0; k < 2; ++k)
                 for (int l = 0; l < 11; ++l) {

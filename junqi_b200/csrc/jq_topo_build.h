@@ -216,4 +216,24 @@ inline void build_slot_topo(const Topo &T, SlotTopo &S) {
     }
 }
 
+// Straight rail rays as cell masks: ray k of cell c (directions +x, -x, +y,
+// -y) holds the cells of T.sray[c][k].  Those cells lie on one axis in strictly
+// increasing (k = 0, 2) or decreasing (k = 1, 3) flat, hence compact, order,
+// which lets a kernel find the first blocker with one bit scan.  Returns
+// false if a ray breaks that order.
+inline bool build_ray_masks(const Topo &T, uint32_t out[NB][4][NW]) {
+    for (int c = 0; c < NB; ++c)
+        for (int k = 0; k < 4; ++k) {
+            for (int i = 0; i < NW; ++i) out[c][k][i] = 0u;
+            int prev = c;
+            for (int l = 0; l < 12 && T.sray[c][k][l] != NONE8; ++l) {
+                const int v = T.sray[c][k][l];
+                if ((k & 1) ? v >= prev : v <= prev) return false;
+                out[c][k][v >> 5] |= 1u << (v & 31);
+                prev = v;
+            }
+        }
+    return true;
+}
+
 }  // namespace jq
