@@ -213,6 +213,72 @@ def reference_arm(args, cfg: dict) -> None:
     print(json.dumps(line), flush=True)
 
 
+def reference_cuda_arm(args, cfg: dict) -> None:
+    """The reference's own CUDA extension on this GPU -- a reported baseline,
+    not part of the driver contract.  Built by baseline/build_ref_cuda.py
+    into baseline/_ref; times the reference ``GpuRollout`` per-ply chain
+    (gpu_collector.py:770-978: acting-seat observation, canonical mask,
+    step_device, belief update, reset of finished games) with CUDA events
+    around those calls only, the action choice (a masked argmax with keys
+    that change every ply) left out."""
+    import glob
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    so = glob.glob(str(ROOT / "baseline" / "_ref" / "junqi_rl" / "junqi_cuda*.so"))
+    if not so:
+        print(json.dumps({"impl": "reference-cuda", "unavailable": "baseline/_ref has no junqi_cuda build; "
+                          "run baseline/build_ref_cuda.py where the reference checkout exists"}), flush=True)
+        return
+    sys.path.insert(0, str(ROOT / "baseline" / "_ref" / "junqi_rl"))
+    sys.path.insert(0, str(ROOT / "baseline" / "_ref"))
+    import torch
+    from junqi_core.rules import ShowMode
+    from junqi_rl.gpu_rollout import GpuRollout, _CudaArrayInterfaceView
+    n, plies = args.envs or cfg["envs"], args.steps or cfg["plies"]
+    if cfg["seats"] != 1:
+        print(json.dumps({"impl": "reference-cuda", "unavailable": "only the acting-seat configs are timed"}))
+        return
+    ro = GpuRollout(num_envs=n, show_mode=ShowMode(cfg["mode"]), device_id=0)
+    ro.reset_from_setup_pool(seed=args.seed)
+    g = torch.Generator(device="cuda").manual_seed(args.seed)
+    keys = torch.randint(1, 32000, (16641,), device="cuda", dtype=torch.int32, generator=g)
+    applied = torch.zeros((), dtype=torch.int64, device="cuda")
+    evs = []
+    for t in range(args.warmup + plies):
+        acting = ro.turn_torch().clone()
+        a = torch.cuda.Event(enable_timing=True)
+        b1 = torch.cuda.Event(enable_timing=True)
+        a.record()
+        ro.build_acting_seat_observation_torch(acting)
+        lm = ro.legal_mask_canonical_torch_device(acting)
+        b1.record()
+        acts = (lm.to(torch.int32) * torch.roll(keys, t)).argmax(dim=1).to(torch.int32)
+        c = torch.cuda.Event(enable_timing=True)
+        d = torch.cuda.Event(enable_timing=True)
+        c.record()
+        res = ro.step_device_torch(acts, acting)
+        ro.update_beliefs_device(res, acting)
+        ro.reset_terminated_device(seed=args.seed + 1_000_003 * (t + 1))
+        d.record()
+        if t >= args.warmup:
+            valid = torch.as_tensor(_CudaArrayInterfaceView(ro._last_step_ptrs["d_valid_ptr"], (n,), "|b1"),
+                                    device="cuda")
+            applied += valid.sum()
+            evs.append((a, b1, c, d))
+    torch.cuda.synchronize()
+    ms = sum(a.elapsed_time(b1) + c.elapsed_time(d) for a, b1, c, d in evs)
+    done = int(applied)
+    print(json.dumps({"impl": "reference-cuda", "metric": "env plies/s (step + legal mask + 317-ch obs)",
+                      "value": done / (ms / 1e3), "unit": "plies/s", "n_gpus": 1, "steps": plies,
+                      "warmup": args.warmup, "ms_per_step": ms / plies, "higher_is_better": True,
+                      "config": {"workload": cfg["workload"], "envs_per_gpu": n, "plies_applied": done,
+                                 "policy": "masked argmax over keys rotated every ply (not timed)",
+                                 "chain": "build_acting_seat_observation_torch, legal_mask_canonical_torch_device, "
+                                          "step_device_torch, update_beliefs_device, reset_terminated_device"},
+                      "source": "reference junqi_cuda built for sm_100a by baseline/build_ref_cuda.py"}), flush=True)
+
+
 # ---------------------------------------------------------------------------
 # GPU arm
 # ---------------------------------------------------------------------------
@@ -222,7 +288,7 @@ def main() -> None:
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=None, help="timed plies (default: the config's plies)")
     ap.add_argument("--warmup", type=int, default=10)
-    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference", "reference-cuda"])
     ap.add_argument("--config", default="cfg2", choices=sorted(CONFIGS))
     ap.add_argument("--envs", type=int, default=None, help="envs per GPU (default: the config's)")
     ap.add_argument("--e2e-steps", type=int, default=100)
@@ -237,6 +303,9 @@ def main() -> None:
         cfg["envs"] = args.envs
     if args.steps is None:
         args.steps = cfg["plies"]
+    if args.impl == "reference-cuda":
+        reference_cuda_arm(args, cfg)
+        return
     if args.impl == "reference":
         reference_arm(args, cfg)
         return
