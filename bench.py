@@ -267,11 +267,15 @@ def reference_cuda_arm(args, cfg: dict) -> None:
             applied += valid.sum()
             evs.append((a, b1, c, d))
     torch.cuda.synchronize()
-    ms = sum(a.elapsed_time(b1) + c.elapsed_time(d) for a, b1, c, d in evs)
+    ms_obs = sum(a.elapsed_time(b1) for a, b1, c, d in evs)
+    ms_step = sum(c.elapsed_time(d) for a, b1, c, d in evs)
+    ms = ms_obs + ms_step
     done = int(applied)
     print(json.dumps({"impl": "reference-cuda", "metric": "env plies/s (step + legal mask + 317-ch obs)",
                       "value": done / (ms / 1e3), "unit": "plies/s", "n_gpus": 1, "steps": plies,
                       "warmup": args.warmup, "ms_per_step": ms / plies, "higher_is_better": True,
+                      "split_ms_per_step": {"observation + canonical mask": ms_obs / plies,
+                                            "step + beliefs + reset": ms_step / plies},
                       "config": {"workload": cfg["workload"], "envs_per_gpu": n, "plies_applied": done,
                                  "policy": "masked argmax over keys rotated every ply (not timed)",
                                  "chain": "build_acting_seat_observation_torch, legal_mask_canonical_torch_device, "
