@@ -16,7 +16,7 @@
 #include <stddef.h>
 #include <stdint.h>
 
-#define JQ_ABI_VERSION 4
+#define JQ_ABI_VERSION 5
 
 #define JQ_NUM_PIECES 120
 #define JQ_NUM_CELLS 289
@@ -92,7 +92,14 @@ typedef struct jq_batch {
     int16_t *remaining;                /* (4,4,12) per-observer enemy inventory */
     uint8_t *rem_tracked;              /* (4,4)  bool */
     int32_t rules;                     /* JQ_RULES_BATCHED or JQ_RULES_GAMESTATE */
+    int32_t max_moves;                 /* episode cap in plies, 0: the rules' 4000 (see below) */
 } jq_batch;
+
+/* jq_batch.max_moves: a game that reaches this many plies without a natural
+ * result ends as a draw, checked after the victory and Q12 rules of the ply
+ * (the reference's DeviceGameStateBatch max_num_moves, game_state.cu:1651-
+ * 1655, like JunqiEnv's episode cap).  0 leaves only the rules' own draw at
+ * move 4000 or 200 plies without combat (rules.py:444). */
 
 /* Per-env step outputs (N each); any pointer may be NULL except valid. */
 typedef struct jq_step_out {

@@ -51,7 +51,8 @@ BYTES_PER_ENV = sum(int(np.dtype(dt).itemsize * np.prod(sh, dtype=np.int64)) for
 class DeviceBatch:
     """N envs of device state in the jq_batch layout."""
 
-    def __init__(self, n: int, device: torch.device | str | int = "cuda", rules: int = N.RULES_BATCHED):
+    def __init__(self, n: int, device: torch.device | str | int = "cuda", rules: int = N.RULES_BATCHED,
+                 max_moves: int = 0):
         if n <= 0:
             raise ValueError(f"num_envs must be positive, got {n}")
         self.n = int(n)
@@ -62,6 +63,7 @@ class DeviceBatch:
         self._struct = N.JqBatch()
         self._struct.n = self.n
         self._struct.rules = int(rules)
+        self.max_moves = max_moves
         for name, _, _, _ in FIELDS:
             setattr(self._struct, name, self.t[name].data_ptr())
 
@@ -76,6 +78,17 @@ class DeviceBatch:
         self._struct.rules = int(r)
 
     @property
+    def max_moves(self) -> int:
+        """Episode cap in plies (a draw when reached), 0 for none beyond the rules' own."""
+        return int(self._struct.max_moves)
+
+    @max_moves.setter
+    def max_moves(self, m: int) -> None:
+        if int(m) < 0:
+            raise ValueError(f"max_moves must be >= 0, got {m}")
+        self._struct.max_moves = int(m)
+
+    @property
     def struct(self) -> N.JqBatch:
         return self._struct
 
@@ -86,6 +99,7 @@ class DeviceBatch:
         s = N.JqBatch()
         s.n = int(count)
         s.rules = self._struct.rules
+        s.max_moves = self._struct.max_moves
         for name, _, _, _ in FIELDS:
             t = self.t[name]
             setattr(s, name, t.data_ptr() + start * t.stride(0) * t.element_size())

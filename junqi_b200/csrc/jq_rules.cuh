@@ -980,6 +980,11 @@ __device__ bool warp_step(const jq_batch &b, const Topo &T, WEnv &w, int e, int 
     }
     __syncwarp();
     if (lane == 0) {
+        // the caller's episode cap, after victory and Q12 (game_state.cu:1651-1655)
+        if (!x.term && b.max_moves > 0 && x.new_mc >= b.max_moves) {
+            x.term = 1;
+            x.draw = 1;
+        }
         zob ^= g_zmc[x.new_mc & 0xFFF] ^ g_zmslc[x.new_mslc & 0x1FF] ^ c_zturn[x.new_turn & 3];
         if (x.term) zob ^= c_zterm;
         if (x.draw) zob ^= c_zdraw;

@@ -56,14 +56,14 @@ class JunqiEnvB200:
     def __init__(self, num_envs: int, *, device: int = 0, show_mode: int = HALF_DARK,
                  pool: np.ndarray | None = None, pool_size: int = 10_000, pool_seed: int = 42,
                  obs_seats: int = 1, legal_cap: int = MAX_LEGAL, with_mask: bool = True,
-                 with_obs: bool = True, rules: int = N.RULES_BATCHED):
+                 with_obs: bool = True, rules: int = N.RULES_BATCHED, max_moves: int = 0):
         ensure_device(device)
         self.device = torch.device("cuda", device)
         self.n = int(num_envs)
         self.show_mode = int(show_mode)
         self.cap = int(legal_cap)
         self.obs_seats = int(obs_seats)
-        self.batch = DeviceBatch(self.n, self.device, rules=rules)
+        self.batch = DeviceBatch(self.n, self.device, rules=rules, max_moves=max_moves)
         if pool is None:
             pool = tables.build_setup_pool(pool_size, seed=pool_seed)
         self.set_pool(pool)

@@ -194,12 +194,14 @@ class DeviceGameStateBatch:
                  rules: int = N.RULES_BATCHED):
         if num_envs <= 0 or num_envs > NUM_ENVS_MAX:
             raise RuntimeError(f"num_envs must be in [1, {NUM_ENVS_MAX}]")
-        if max_num_moves != 4000:
-            raise RuntimeError("max_num_moves other than 4000 is not supported (BatchedGameState rule)")
+        if max_num_moves <= 0:
+            raise RuntimeError("max_num_moves must be positive")
         ensure_device(_device)
         self.num_envs = int(num_envs)
         self.show_mode = int(show_mode)
-        self.b = DeviceBatch(self.num_envs, f"cuda:{_device}", rules=rules)
+        # the rules draw at move 4000 by themselves; a shorter cap ends games as draws earlier
+        self.b = DeviceBatch(self.num_envs, f"cuda:{_device}", rules=rules,
+                             max_moves=0 if max_num_moves >= 4000 else int(max_num_moves))
         n, dev = self.num_envs, self.b.device
         self._out = {k: torch.zeros(n, dtype=dt, device=dev) for k, dt in
                      (("valid", torch.uint8), ("event", torch.int8), ("terminated", torch.uint8),

@@ -1146,6 +1146,8 @@ static void step_env(jqo_batch *b, int e, int32_t act, int mode, jqo_step_out *o
             new_turn = acting;
         }
     }
+    /* the caller's episode cap, after victory and Q12 (game_state.cu:1651-1655) */
+    if (!term && b->max_moves > 0 && new_mc >= b->max_moves) { term = 1; draw = 1; }
     zob ^= Z_mc[new_mc & 0xFFF] ^ Z_mslc[new_mslc & 0x1FF] ^ Z_turn[new_turn];
     if (term) zob ^= Z_term;
     if (draw) zob ^= Z_draw;

@@ -70,6 +70,7 @@ typedef struct {
     int16_t *remaining;
     uint8_t *rem_tracked;
     int32_t rules; /* 0: BatchedGameState rules, 1: GameState rules */
+    int32_t max_moves; /* episode cap in plies (draw), 0: none beyond the rules' 4000 */
 } jqo_batch;
 
 /* Per-step outputs (n,) */

@@ -94,7 +94,7 @@ _CTYPE = {
 class _CBatch(ctypes.Structure):
     _fields_ = [("n", ctypes.c_int32)] + [
         (name, ctypes.POINTER(_CTYPE[dt])) for name, dt, _, _ in FIELDS
-    ] + [("rules", ctypes.c_int32)]
+    ] + [("rules", ctypes.c_int32), ("max_moves", ctypes.c_int32)]
 
 
 class _CStepOut(ctypes.Structure):

@@ -121,3 +121,25 @@ def test_explicit_observer_lists():
     for j in range(3):
         o_sp, o_gl = orc.obs(obs[:, j].copy())
         assert np.array_equal(sp[:, j], o_sp) and np.array_equal(gl[:, j], o_gl), j
+
+
+@pytest.mark.parametrize("rules", [N.RULES_BATCHED, N.RULES_GAMESTATE])
+def test_episode_cap_draws_like_the_oracle(rules):
+    """jq_batch.max_moves: games reaching the cap end as draws (after the
+    ply's own victory and Q12 rules), with auto-resets continuing."""
+    env, orc, pool = _pair(24, 17, rules=rules, max_moves=23)
+    orc._c.max_moves = 23
+    L = N.lib()
+    draws = 0
+    for t in range(1, 120):
+        acts = env.sample_uniform(17, t)
+        a = acts.cpu().numpy().copy()
+        out = env.ply(acts, seed=17, ply=t)
+        r = orc.step(a)
+        for k in ("valid", "terminated", "winner", "draw", "reward"):
+            assert np.array_equal(out[k].cpu().numpy().astype(r[k].dtype), r[k]), (t, k)
+        draws += int(r["draw"].sum())
+        for e in np.nonzero(r["terminated"])[0]:
+            orc.reset_env(int(e), pool[L.jq_pool_index(17, t, int(e), pool.shape[0])])
+        _compare_state(env, orc, t)
+    assert draws >= 24
