@@ -15,7 +15,7 @@
 //
 // Persistent CTAs of 12 warps, specialised:
 //  * 4 staging warps take units in memory order through an atomic ticket
-//    (two units ahead) and build unit k+1 in one of two shared
+//    and build unit k+1 in one of two shared
 //    buffers: warp w takes the 30 pieces of seat o + w, thread = piece,
 //    setting the bits the piece lights at its canonical cell with shared
 //    atomicOr and filling its record; then history, constant and
@@ -119,7 +119,7 @@ struct __align__(16) ObsSmem {
     UnitBuf buf[2];
     int16_t rotf[4][NC];                // world flat -> canonical flat, per observer seat
     uint32_t statw[4][4][STAT_WORDS];   // board-static bits as stream words, per observer and stream offset
-    int ticket[2], next_o[2];  // the staging warps' next two units and their observers
+    int ticket[1], next_o[1];  // the staging warps' next unit and its observer
     float prior[30 * 12], uniform[12];  // belief tables: global loads here would wait behind the write stream
     int8_t slot_ch[30];
 };
@@ -566,17 +566,18 @@ __global__ void __launch_bounds__(OBS_THREADS, OBS_MIN_CTAS) obs_kernel(jq_batch
         }
     } else {
         const int t = tid - 32 * OBS_STREAM_WARPS;
-        // The next unit (and its observer) is fetched while the current one
-        // is staged, so the ticket and observer loads leave the critical path.
+        // A unit is taken only when the staging warps are ready to build it:
+        // the units being written at any moment then stay in the tightest
+        // window of the output, and no CTA holds a unit it has not started
+        // when the tickets run out (a reservation one unit ahead measured
+        // 1 % slower at both 4,096 and 65,536 units).
         if (t == 0) {
-            const int u0 = atomicAdd(&ticket[0], 2);
+            const int u0 = atomicAdd(&ticket[0], 1);
             S.ticket[0] = u0;
             S.next_o[0] = u0 < units ? unit_observer(b, observers, seats, u0) : 0;
-            S.ticket[1] = u0 + 1;
-            S.next_o[1] = u0 + 1 < units ? unit_observer(b, observers, seats, u0 + 1) : 0;
         }
         bar_sync(BAR_STAGE, OBS_STAGE_THREADS);
-        int u = S.ticket[0], o = S.next_o[0], u1 = S.ticket[1], o1 = S.next_o[1];
+        int u = S.ticket[0], o = S.next_o[0];
         int k = 0;
         for (;; ++k) {
             const int bi = k & 1;
@@ -587,20 +588,17 @@ __global__ void __launch_bounds__(OBS_THREADS, OBS_MIN_CTAS) obs_kernel(jq_batch
                 bar_arrive(BAR_FULL0 + bi, OBS_THREADS);
                 break;
             }
-            int un = 0, on = 0;
-            if (t == 0) {
-                un = atomicAdd(&ticket[0], 1);
-                on = un < units ? unit_observer(b, observers, seats, un) : 0;
-            }
             stage_unit(b, seats, mode, ext_bel, global, S, B, u, o, unit_head(spatial, u), t, BAR_STAGE);
-            if (t == 0) { S.ticket[0] = un; S.next_o[0] = on; }
-            bar_sync(BAR_STAGE, OBS_STAGE_THREADS);  // unit staged; the ticket after next published
-            u = u1;
-            o = o1;
-            u1 = S.ticket[0];
-            o1 = S.next_o[0];
-            bar_arrive(BAR_FULL0 + bi, OBS_THREADS);
-            bar_sync(BAR_STAGE, OBS_STAGE_THREADS);  // everyone has read the next ticket
+            bar_sync(BAR_STAGE, OBS_STAGE_THREADS);    // unit staged by every staging thread
+            bar_arrive(BAR_FULL0 + bi, OBS_THREADS);  // hand it to the streaming warps
+            if (t == 0) {
+                const int un = atomicAdd(&ticket[0], 1);
+                S.ticket[0] = un;
+                S.next_o[0] = un < units ? unit_observer(b, observers, seats, un) : 0;
+            }
+            bar_sync(BAR_STAGE, OBS_STAGE_THREADS);  // next ticket published
+            u = S.ticket[0];
+            o = S.next_o[0];
         }
         if (k >= 1) bar_sync(BAR_EMPTY0 + ((k - 1) & 1), OBS_THREADS);  // the last unit has been streamed
         if (t == 0) {
