@@ -13,10 +13,10 @@
 // floats, so its base is only 4-byte aligned); every aligned float4 of the
 // output then owns one 4-bit nibble of a 32-bit word.
 //
-// Persistent CTAs of 12 warps, specialised:
-//  * 4 staging warps take units in memory order through an atomic ticket
+// Persistent CTAs of 16 warps, specialised:
+//  * 8 staging warps take units in memory order through an atomic ticket
 //    and build unit k+1 in one of two shared
-//    buffers: warp w takes the 30 pieces of seat o + w, thread = piece,
+//    buffers: warps w and w + 4 split the 30 pieces of seat o + w, thread = piece,
 //    setting the bits the piece lights at its canonical cell with shared
 //    atomicOr and filling its record; then history, constant and
 //    board-static planes; the globals go straight to HBM;
@@ -47,8 +47,9 @@
 namespace jq {
 
 constexpr int OBS_STREAM_WARPS = 8;
-constexpr int OBS_STAGE_WARPS = 4;
-constexpr int OBS_STAGE_THREADS = 32 * OBS_STAGE_WARPS;                      // 128 >= 120 pieces
+constexpr int OBS_STAGE_WARPS = 8;  // two per seat relation
+constexpr int OBS_STAGE_THREADS = 32 * OBS_STAGE_WARPS;                      // 256
+static_assert(OBS_STAGE_WARPS % 4 == 0, "staging warps come in groups of four seat relations");
 constexpr int OBS_THREADS = 32 * (OBS_STREAM_WARPS + OBS_STAGE_WARPS);      // 384
 constexpr int OBS_WORDS = (OBS_FLOATS + 8 + 31) / 32;  // 2,864 words per stream
 constexpr int OBS_WORDS4 = (OBS_WORDS + 3) / 4;         // in uint4
@@ -407,12 +408,14 @@ __device__ void stage_unit(const jq_batch &b, int seats, int mode, const float *
     }
     bar_sync(bar_stage, OBS_STAGE_THREADS);
     // pieces, then history / constants / statics (all bit writes are atomic)
-    {  // staging warp w takes the 30 pieces of seat o + w: one seat relation per warp
-        const int ln = t & 31;
-        const int p = ((o + (t >> 5)) & 3) * 30 + ln;
-        if (ln < 30) stage_piece(b, e, o, mode, S, st, p);
+    {  // staging warp w takes a share of the pieces of seat o + w % 4: one seat relation per warp
+        constexpr int wps = OBS_STAGE_WARPS / 4, per = (30 + wps - 1) / wps;
+        const int ln = t & 31, wi = t >> 5, slot = (wi >> 2) * per + ln;
+        const bool mine = ln < per && slot < 30;
+        const int p = ((o + (wi & 3)) & 3) * 30 + (mine ? slot : 0);
+        if (mine) stage_piece(b, e, o, mode, S, st, p);
         // list the pieces holding records, one shared atomic per warp and list
-        const bool rec = ln < 30 && B.pcell[p] >= 0;
+        const bool rec = mine && B.pcell[p] >= 0;
         const uint32_t fl = rec ? B.pflag[p] : 0u, below = (1u << ln) - 1u;
         const uint32_t mb = __ballot_sync(0xffffffffu, fl & 1u), mc = __ballot_sync(0xffffffffu, fl & 2u);
         int bb = 0, bc = 0;
