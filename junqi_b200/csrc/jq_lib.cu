@@ -68,12 +68,22 @@ __global__ void rotate_actions_kernel(int n, const int32_t *can, const int8_t *s
 }
 
 // ---------------------------------------------------------------------------
-// CSR: block sums, then per-block exclusive scan + value compaction
+// CSR: block sums, per-block exclusive scan, then value compaction with one
+// warp per env (every env's copy in flight at once)
 // ---------------------------------------------------------------------------
-constexpr int CSR_BLOCK = 1024;
+constexpr int CSR_BLOCK = 1024;   // envs per block sum
+constexpr int CSR_COPY_WARPS = 8; // envs per block of csr_values_kernel
+
+// Launched with programmatic dependent launch: wait for the kernel that wrote
+// the counts and ids, let the next kernel in the stream be scheduled early.
+__device__ __forceinline__ void csr_pdl_enter() {
+    asm volatile("griddepcontrol.launch_dependents;");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
 
 __global__ void csr_partial_kernel(int n, const int32_t *counts, int cap, int32_t *partial) {
     __shared__ int32_t red[32];
+    csr_pdl_enter();
     int e = blockIdx.x * CSR_BLOCK + threadIdx.x;
     int v = e < n ? min(counts[e], cap) : 0;
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(FULL, v, o);
@@ -86,19 +96,20 @@ __global__ void csr_partial_kernel(int n, const int32_t *counts, int cap, int32_
     }
 }
 
-__global__ void csr_finalize_kernel(int n, const int32_t *counts, const int32_t *ids, int cap,
-                                    const int32_t *partial, int32_t *offsets, int32_t *values) {
+__global__ void csr_offsets_kernel(int n, const int32_t *counts, int cap, const int32_t *partial,
+                                   int32_t *offsets) {
     __shared__ int32_t wsum[32];
     __shared__ int32_t base_s;
-    __shared__ int32_t offs[CSR_BLOCK];
-    if (threadIdx.x == 0) {
+    csr_pdl_enter();
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    if (wid == 0) {  // sum of the block sums before this block
         int s = 0;
-        for (int k = 0; k < (int)blockIdx.x; ++k) s += partial[k];
-        base_s = s;
+        for (int k = lane; k < (int)blockIdx.x; k += 32) s += partial[k];
+        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(FULL, s, o);
+        if (lane == 0) base_s = s;
     }
     int e = blockIdx.x * CSR_BLOCK + threadIdx.x;
-    int v = e < n ? min(counts[e], cap) : 0;
-    int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, inc = v;
+    int v = e < n ? min(counts[e], cap) : 0, inc = v;
     for (int o = 1; o < 32; o <<= 1) {
         int t = __shfl_up_sync(FULL, inc, o);
         if (lane >= o) inc += t;
@@ -115,17 +126,18 @@ __global__ void csr_finalize_kernel(int n, const int32_t *counts, const int32_t 
     }
     __syncthreads();
     int excl = base_s + wsum[wid] + inc - v;
-    offs[threadIdx.x] = excl;
     if (e < n) offsets[e] = excl;
     if (e == n - 1) offsets[n] = excl + v;
-    __syncthreads();
-    // one warp per env copies its ids
-    for (int k = wid; k < CSR_BLOCK; k += 32) {
-        int ee = blockIdx.x * CSR_BLOCK + k;
-        if (ee >= n) break;
-        int c = min(counts[ee], cap), o = offs[k];
-        for (int j = lane; j < c; j += 32) values[o + j] = ids[(size_t)ee * cap + j];
-    }
+}
+
+__global__ void csr_values_kernel(int n, const int32_t *counts, const int32_t *ids, int cap,
+                                  const int32_t *offsets, int32_t *values) {
+    csr_pdl_enter();
+    const int lane = threadIdx.x & 31;
+    const int e = blockIdx.x * CSR_COPY_WARPS + (threadIdx.x >> 5);
+    if (e >= n) return;
+    const int c = min(counts[e], cap), o = offsets[e];
+    for (int j = lane; j < c; j += 32) values[o + j] = ids[(size_t)e * cap + j];
 }
 
 // ---------------------------------------------------------------------------
@@ -270,6 +282,19 @@ static int launch_rules(RuleArgs &a, cudaStream_t s) {
     int cap_blocks = st->sms * (st->rule_blocks_per_sm > 0 ? st->rule_blocks_per_sm : 1) * 4;
     if (blocks > cap_blocks) blocks = cap_blocks;
     CU(launch_pdl(rules_kernel, (unsigned)blocks, RULE_THREADS, rule_smem(), s, a));
+    return JQ_OK;
+}
+
+// The three CSR kernels; scratch holds ceil(n / CSR_BLOCK) block sums, all
+// written by csr_partial_kernel before csr_offsets_kernel reads them.
+static int launch_csr(int32_t n, const int32_t *counts, const int32_t *ids, int32_t cap, int32_t *scratch,
+                      int32_t *offsets, int32_t *values, cudaStream_t s) {
+    const unsigned blocks = (unsigned)((n + CSR_BLOCK - 1) / CSR_BLOCK);
+    CU(launch_pdl(csr_partial_kernel, blocks, CSR_BLOCK, 0, s, (int)n, counts, (int)cap, scratch));
+    CU(launch_pdl(csr_offsets_kernel, blocks, CSR_BLOCK, 0, s, (int)n, counts, (int)cap,
+                  (const int32_t *)scratch, offsets));
+    CU(launch_pdl(csr_values_kernel, (unsigned)((n + CSR_COPY_WARPS - 1) / CSR_COPY_WARPS), 32 * CSR_COPY_WARPS, 0,
+                  s, (int)n, counts, ids, (int)cap, (const int32_t *)offsets, values));
     return JQ_OK;
 }
 
@@ -574,13 +599,7 @@ int jq_csr(int32_t n, const int32_t *d_counts, const int32_t *d_ids, int32_t cap
            int32_t *d_values, int32_t *d_block_scratch, void *stream) {
     if (n <= 0 || !d_counts || !d_ids || !d_offsets || !d_values || !d_block_scratch || cap <= 0)
         return fail(JQ_ERR_ARG, "bad CSR arguments");
-    int blocks = jq_csr_scratch_ints(n);
-    cudaStream_t s = (cudaStream_t)stream;
-    csr_partial_kernel<<<blocks, CSR_BLOCK, 0, s>>>(n, d_counts, cap, d_block_scratch);
-    CU(cudaGetLastError());
-    csr_finalize_kernel<<<blocks, CSR_BLOCK, 0, s>>>(n, d_counts, d_ids, cap, d_block_scratch, d_offsets, d_values);
-    CU(cudaGetLastError());
-    return JQ_OK;
+    return launch_csr(n, d_counts, d_ids, cap, d_block_scratch, d_offsets, d_values, (cudaStream_t)stream);
 }
 
 // ---------------------------------------------------------------------------
@@ -617,15 +636,9 @@ int jq_csr_noalloc(int32_t n, const int32_t *d_counts, const int32_t *d_ids, int
         }
         scratch = g_noalloc_ptr[dev];
     }
-    // csr_partial_kernel writes every block sum csr_finalize_kernel reads, so
+    // csr_partial_kernel writes every block sum csr_offsets_kernel reads, so
     // the contents left by the previous call need no clearing.
-    int blocks = jq_csr_scratch_ints(n);
-    cudaStream_t s = (cudaStream_t)stream;
-    csr_partial_kernel<<<blocks, CSR_BLOCK, 0, s>>>(n, d_counts, cap, scratch);
-    CU(cudaGetLastError());
-    csr_finalize_kernel<<<blocks, CSR_BLOCK, 0, s>>>(n, d_counts, d_ids, cap, scratch, d_offsets, d_values);
-    CU(cudaGetLastError());
-    return JQ_OK;
+    return launch_csr(n, d_counts, d_ids, cap, scratch, d_offsets, d_values, (cudaStream_t)stream);
 }
 
 static int observe_launch(const jq_batch *b, const int8_t *d_observers, int32_t seats_per_env, int32_t show_mode,
