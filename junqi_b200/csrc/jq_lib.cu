@@ -48,9 +48,19 @@ __global__ void rehash_kernel(jq_batch b, int mode) {
     }
 }
 
+// Entry of the small kernels launched with programmatic dependent launch
+// (launch_pdl): let the next kernel in the stream be scheduled early, then
+// wait until the previous one has completed and its writes are visible,
+// before the first access to caller memory.
+__device__ __forceinline__ void pdl_enter() {
+    asm volatile("griddepcontrol.launch_dependents;");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 // compact canonical action -> world flat action (game_state.cu:2639-2685 semantics)
 __global__ void rotate_actions_kernel(int n, const int32_t *can, const int8_t *seats, const int8_t *turn,
                                       int32_t *world) {
+    pdl_enter();
     int e = blockIdx.x * blockDim.x + threadIdx.x;
     if (e >= n) return;
     int a = can[e];
@@ -74,16 +84,9 @@ __global__ void rotate_actions_kernel(int n, const int32_t *can, const int8_t *s
 constexpr int CSR_BLOCK = 1024;   // envs per block sum
 constexpr int CSR_COPY_WARPS = 8; // envs per block of csr_values_kernel
 
-// Launched with programmatic dependent launch: wait for the kernel that wrote
-// the counts and ids, let the next kernel in the stream be scheduled early.
-__device__ __forceinline__ void csr_pdl_enter() {
-    asm volatile("griddepcontrol.launch_dependents;");
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-}
-
 __global__ void csr_partial_kernel(int n, const int32_t *counts, int cap, int32_t *partial) {
     __shared__ int32_t red[32];
-    csr_pdl_enter();
+    pdl_enter();
     int e = blockIdx.x * CSR_BLOCK + threadIdx.x;
     int v = e < n ? min(counts[e], cap) : 0;
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(FULL, v, o);
@@ -100,7 +103,7 @@ __global__ void csr_offsets_kernel(int n, const int32_t *counts, int cap, const 
                                    int32_t *offsets) {
     __shared__ int32_t wsum[32];
     __shared__ int32_t base_s;
-    csr_pdl_enter();
+    pdl_enter();
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     if (wid == 0) {  // sum of the block sums before this block
         int s = 0;
@@ -132,7 +135,7 @@ __global__ void csr_offsets_kernel(int n, const int32_t *counts, int cap, const 
 
 __global__ void csr_values_kernel(int n, const int32_t *counts, const int32_t *ids, int cap,
                                   const int32_t *offsets, int32_t *values) {
-    csr_pdl_enter();
+    pdl_enter();
     const int lane = threadIdx.x & 31;
     const int e = blockIdx.x * CSR_COPY_WARPS + (threadIdx.x >> 5);
     if (e >= n) return;
@@ -145,6 +148,7 @@ __global__ void csr_values_kernel(int n, const int32_t *counts, const int32_t *i
 // ---------------------------------------------------------------------------
 __global__ void sample_uniform_kernel(int n, const int32_t *counts, const int32_t *ids, int cap, uint64_t seed,
                                       uint64_t ply, int32_t *acts) {
+    pdl_enter();
     int e = blockIdx.x * blockDim.x + threadIdx.x;
     if (e >= n) return;
     int c = min(counts[e], cap);
@@ -159,6 +163,7 @@ __device__ __forceinline__ float u01(uint64_t h) {  // (0, 1)
 // (Box-Muller) and G ~ Gumbel(0,1), both keyed on (seed, ply, env, action).
 __global__ void sample_softmax_kernel(int n, const int8_t *turn, const int32_t *counts, const int32_t *ids, int cap,
                                       uint64_t seed, uint64_t ply, int32_t *can_out, int32_t *world_out) {
+    pdl_enter();
     int e = blockIdx.x * blockDim.x + threadIdx.x;
     if (e >= n) return;
     int c = min(counts[e], cap), seat = turn[e] & 3;
@@ -512,9 +517,8 @@ int jq_step_canonical(const jq_batch *b, const int32_t *d_compact_actions, const
     if (!out || !out->world_action || !d_compact_actions) return fail(JQ_ERR_ARG, "world_action output required");
     int rc = check_batch(b);
     if (rc) return rc;
-    rotate_actions_kernel<<<(b->n + 255) / 256, 256, 0, (cudaStream_t)stream>>>(b->n, d_compact_actions, d_seats,
-                                                                             b->turn, out->world_action);
-    CU(cudaGetLastError());
+    CU(launch_pdl(rotate_actions_kernel, (unsigned)((b->n + 255) / 256), 256, 0, (cudaStream_t)stream, (int)b->n,
+                  d_compact_actions, d_seats, (const int8_t *)b->turn, out->world_action));
     return jq_step(b, out->world_action, show_mode, out, stream);
 }
 
@@ -523,9 +527,8 @@ int jq_canonical_to_world(const jq_batch *b, const int32_t *d_compact_actions, c
     int rc = check_batch(b);
     if (rc) return rc;
     if (!d_compact_actions || !d_world_actions) return fail(JQ_ERR_ARG, "actions missing");
-    rotate_actions_kernel<<<(b->n + 255) / 256, 256, 0, (cudaStream_t)stream>>>(b->n, d_compact_actions, d_seats,
-                                                                             b->turn, d_world_actions);
-    CU(cudaGetLastError());
+    CU(launch_pdl(rotate_actions_kernel, (unsigned)((b->n + 255) / 256), 256, 0, (cudaStream_t)stream, (int)b->n,
+                  d_compact_actions, d_seats, (const int8_t *)b->turn, d_world_actions));
     return JQ_OK;
 }
 
@@ -680,18 +683,16 @@ int jq_observe_beliefs(const jq_batch *b, const int8_t *d_observers, int32_t sea
 int jq_sample_uniform(int32_t n, const int32_t *d_counts, const int32_t *d_ids, int32_t cap, uint64_t seed,
                       uint64_t ply, int32_t *d_actions, void *stream) {
     if (n <= 0 || !d_counts || !d_ids || !d_actions || cap <= 0) return fail(JQ_ERR_ARG, "bad sampler arguments");
-    sample_uniform_kernel<<<(n + 255) / 256, 256, 0, (cudaStream_t)stream>>>(n, d_counts, d_ids, cap, seed, ply,
-                                                                            d_actions);
-    CU(cudaGetLastError());
+    CU(launch_pdl(sample_uniform_kernel, (unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream, (int)n, d_counts,
+                  d_ids, (int)cap, seed, ply, d_actions));
     return JQ_OK;
 }
 
 int jq_sample_softmax(const jq_batch *b, const int32_t *d_counts, const int32_t *d_ids, int32_t cap, uint64_t seed,
                       uint64_t ply, int32_t *d_compact_actions, int32_t *d_world_actions, void *stream) {
     if (!b || b->n <= 0 || !b->turn || !d_counts || !d_ids || cap <= 0) return fail(JQ_ERR_ARG, "bad sampler arguments");
-    sample_softmax_kernel<<<(b->n + 127) / 128, 128, 0, (cudaStream_t)stream>>>(
-        b->n, b->turn, d_counts, d_ids, cap, seed, ply, d_compact_actions, d_world_actions);
-    CU(cudaGetLastError());
+    CU(launch_pdl(sample_softmax_kernel, (unsigned)((b->n + 127) / 128), 128, 0, (cudaStream_t)stream, (int)b->n,
+                  (const int8_t *)b->turn, d_counts, d_ids, (int)cap, seed, ply, d_compact_actions, d_world_actions));
     return JQ_OK;
 }
 

@@ -57,8 +57,12 @@ struct StepCtx {
     int died_pre[4];
 };
 
+// words of the canonical-mask bitstream: 16,641 bits, plus one zero word so
+// a 16-bit window starting in the last word can read its successor
+constexpr int CBW = (MASK_BYTES + 31) / 32 + 1;
+
 struct __align__(16) WEnv {
-    uint32_t canon[NB][NW];  // canonical-frame destination rows for the mask
+    uint32_t cbits[CBW];     // the canonical mask as one row-major bitstream (bit j = mask byte j)
     int32_t scan[32];
     StepCtx x;
     int16_t cell[NC + 1];    // flat cell -> pid
@@ -285,21 +289,14 @@ __device__ bool warp_has_moves(const Topo &T, const WEnv &w, int lane, int seat)
     return __any_sync(FULL, any);
 }
 
-// n <= 16 bits of canonical row `row` starting at column col (0 past the row).
-__device__ __forceinline__ uint32_t row_bits(const WEnv &w, int row, int col, int n) {
-    if (row >= NB || n <= 0) return 0u;
-    const int wi = col >> 5;
-    const uint32_t lo = w.canon[row][wi], hi = wi + 1 < NW ? w.canon[row][wi + 1] : 0u;
-    return __funnelshift_r(lo, hi, col & 31) & ((1u << n) - 1u);
-}
-
 // 4 mask bits -> 4 bytes of 0/1 (bit i -> byte i).
 __device__ __forceinline__ uint32_t nibble_bytes(uint32_t nib) { return (nib * 0x00204081u) & 0x01010101u; }
 
-// 16 mask bytes starting at byte j0 = row * 129 + col of the canonical mask.
-__device__ __forceinline__ uint4 mask_chunk(const WEnv &w, int row, int col) {
-    const int n0 = NB - col < 16 ? NB - col : 16;
-    const uint32_t bits = row_bits(w, row, col, n0) | (row_bits(w, row + 1, 0, 16 - n0) << n0);
+// Mask bytes j0 .. j0 + 15 from the bitstream.
+__device__ __forceinline__ uint4 mask_chunk(const WEnv &w, int j0) {
+    const int wi = j0 >> 5;
+    const uint32_t bits = __funnelshift_r(w.cbits[wi], w.cbits[wi + 1], j0 & 31) & 0xffffu;
+    if (!bits) return make_uint4(0u, 0u, 0u, 0u);
     return make_uint4(nibble_bytes(bits & 15u), nibble_bytes((bits >> 4) & 15u), nibble_bytes((bits >> 8) & 15u),
                       nibble_bytes(bits >> 12));
 }
@@ -353,49 +350,30 @@ __device__ int warp_legal(const Topo &T, WEnv &w, int lane, int seat, bool skip,
         }
     }
     if (mask_env) {
-        for (int k = lane; k < NB * NW; k += 32) (&w.canon[0][0])[k] = 0u;
-        // rows (canonical sources) that hold at least one destination
-        uint32_t rows[NW];
-        const int myrow = (src >= 0 && cnt > 0) ? T.rot[seat][src] : -1;
-#pragma unroll
-        for (int i = 0; i < NW; ++i)
-            rows[i] = __reduce_or_sync(FULL, (myrow >= 0 && (myrow >> 5) == i) ? (1u << (myrow & 31)) : 0u);
+        for (int k = lane; k < CBW; k += 32) w.cbits[k] = 0u;
         __syncwarp();
         if (src >= 0) {
-            uint32_t *row = w.canon[T.rot[seat][src]];
+            // bit (canonical source row) * 129 + canonical destination; rows
+            // of two lanes can share a word, hence the atomic
+            const int rb = T.rot[seat][src] * NB;
 #pragma unroll
             for (int i = 0; i < NW; ++i) {
                 uint32_t m = d[i];
                 while (m) {
-                    int dc = i * 32 + __ffs(m) - 1;
+                    const int j = rb + T.rot[seat][i * 32 + __ffs(m) - 1];
                     m &= m - 1;
-                    mset(row, T.rot[seat][dc]);
+                    atomicOr(&w.cbits[j >> 5], 1u << (j & 31));
                 }
             }
         }
         __syncwarp();
-        int head = (int)((16 - ((uintptr_t)mask_env & 15)) & 15);
-        for (int j = lane; j < head; j += 32) {
-            int row = j / NB, col = j - row * NB;
-            mask_env[j] = (uint8_t)((w.canon[row][col >> 5] >> (col & 31)) & 1u);
-        }
-        int body = (MASK_BYTES - head) >> 4;
-        // lane k writes chunks k, k + 32, ...: byte j0 = head + 16 k, advancing
-        // 512 bytes = 3 rows + 125 columns per step
-        int j0 = head + lane * 16;
-        int row = j0 / NB, col = j0 - row * NB;
-        for (int k = lane; k < body; k += 32) {
-            const int row2 = col + 15 >= NB ? row + 1 : row;
-            const bool any = rbit(rows, row) || (row2 < NB && rbit(rows, row2));
-            *reinterpret_cast<uint4 *>(mask_env + head + k * 16) = any ? mask_chunk(w, row, col) : make_uint4(0u, 0u, 0u, 0u);
-            col += 512 - 3 * NB;
-            row += 3;
-            if (col >= NB) { col -= NB; ++row; }
-        }
-        for (int j = head + body * 16 + lane; j < MASK_BYTES; j += 32) {
-            int row = j / NB, col = j - row * NB;
-            mask_env[j] = (uint8_t)((w.canon[row][col >> 5] >> (col & 31)) & 1u);
-        }
+        const int head = (int)((16 - ((uintptr_t)mask_env & 15)) & 15);
+        for (int j = lane; j < head; j += 32) mask_env[j] = (uint8_t)((w.cbits[j >> 5] >> (j & 31)) & 1u);
+        const int body = (MASK_BYTES - head) >> 4;
+        for (int k = lane; k < body; k += 32)
+            *reinterpret_cast<uint4 *>(mask_env + head + k * 16) = mask_chunk(w, head + k * 16);
+        for (int j = head + body * 16 + lane; j < MASK_BYTES; j += 32)
+            mask_env[j] = (uint8_t)((w.cbits[j >> 5] >> (j & 31)) & 1u);
         __syncwarp();
     }
     return total;
