@@ -52,7 +52,7 @@ __device__ __forceinline__ void stage_topo(Topo &dst_t, int tid, int nthreads) {
 __device__ bool warp_ply_env(const RuleArgs &a, const Topo &T, WEnv &w, int e, int lane) {
     const jq_batch &b = a.b;
     bool applied = false;
-    warp_load(b, T, w, e, lane);
+    warp_load(b, T, w, e, lane, (a.flags & DO_STEP) != 0);
     if (a.flags & DO_BELIEF_INIT) {
         warp_belief_init(b, T, w, e, lane, a.mode);
         b.hist_src[(size_t)e * HIST + lane] = -1;

@@ -63,6 +63,8 @@ constexpr int CBW = (MASK_BYTES + 31) / 32 + 1;
 
 struct __align__(16) WEnv {
     uint32_t cbits[CBW];     // the canonical mask as one row-major bitstream (bit j = mask byte j)
+    alignas(16) uint8_t bel[4 * NP];  // belief codes (observer-major), loaded with the state for a step
+    uint64_t cmv[4][4];      // V's combat-memory sets per observer: direct lo/hi, chain lo/hi
     int32_t scan[32];
     StepCtx x;
     int16_t cell[NC + 1];    // flat cell -> pid
@@ -82,8 +84,9 @@ __device__ __forceinline__ size_t PI(int e, int p) { return (size_t)e * NP + p; 
 __device__ __forceinline__ size_t OI(int e, int o, int p) { return ((size_t)e * 4 + o) * NP + p; }
 
 // Every load is issued before any shared-memory store, so the warp waits
-// for global memory once.
-__device__ void warp_load(const jq_batch &b, const Topo &T, WEnv &w, int e, int lane) {
+// for global memory once.  with_bel: also the env's 480 belief codes, read
+// and rewritten by the step's belief update.
+__device__ void warp_load(const jq_batch &b, const Topo &T, WEnv &w, int e, int lane, bool with_bel) {
     constexpr int CI = (NC + 31) / 32, PIT = (NP + 31) / 32;
     int cp[CI];
 #pragma unroll
@@ -104,6 +107,8 @@ __device__ void warp_load(const jq_batch &b, const Topo &T, WEnv &w, int e, int 
             py[i] = b.pos_y[q];
         }
     }
+    uint4 bel = make_uint4(0u, 0u, 0u, 0u);
+    if (with_bel && lane < 4 * NP / 16) bel = reinterpret_cast<const uint4 *>(b.bel_code + OI(e, 0, 0))[lane];
     int64_t sc = 0;
     switch (lane) {
     case 0: sc = b.terminated[e]; break;
@@ -146,6 +151,7 @@ __device__ void warp_load(const jq_batch &b, const Topo &T, WEnv &w, int e, int 
     case 12: case 13: case 14: case 15: w.sflag[lane - 12] = (uint8_t)sc; break;
     default: break;
     }
+    if (with_bel && lane < 4 * NP / 16) reinterpret_cast<uint4 *>(w.bel)[lane] = bel;
     __syncwarp();
 }
 
@@ -466,38 +472,81 @@ __device__ __forceinline__ int next_floor(int t) {
 // lanes 0..29 take the reverse projection onto pid o * 30 + lane of every
 // observer o (reads V's rows, writes eaten-by rows).  The per-observer order
 // of the scalar statement is kept; the three parts commute (OR / max
-// updates of different rows).
-__device__ void warp_cm_apply(const jq_batch &b, int e, int lane, bool eat, int A, int D, int A_seat, int D_seat,
-                              int A_type, int D_type, int step) {
+// updates of different rows), and none reads a row another one writes, so
+// every load is issued before the first store: V's sets go through shared
+// memory (one word per lane), then K's rows and the eaten-by rows are read
+// together.
+__device__ void warp_cm_apply(const jq_batch &b, WEnv &w, int e, int lane, bool eat, int A, int D, int A_seat,
+                              int D_seat, int A_type, int D_type, int step) {
     const int K = eat ? A : D, V = eat ? D : A, V_seat = eat ? D_seat : A_seat, V_type = eat ? D_type : A_type;
     const int v_idx = tracked_idx(V_type);
+    if (lane < 16) {
+        const int o = lane >> 2, f = lane & 3;
+        const uint64_t *src = f == 0 ? b.cm_direct_lo : f == 1 ? b.cm_direct_hi : f == 2 ? b.cm_chain_lo : b.cm_chain_hi;
+        w.cmv[o][f] = src[OI(e, o, V)];
+    }
+    __syncwarp();
+    // loads: K's row of observer o = lane (lanes 0..3) ...
+    const int o4 = lane & 3;
+    const size_t k = OI(e, o4, K), v = OI(e, o4, V);
+    uint8_t g_v = 0;
+    uint64_t ck_lo = 0, ck_hi = 0, dk_lo = 0, dk_hi = 0;
+    uint16_t ck_t = 0, dv_t = 0, cv_t = 0, dk_t = 0;
+    int floor_k = 0, vf = 0, dother = 0;
+    if (lane < 4) {
+        g_v = b.cm_is_gongb[v];
+        ck_lo = b.cm_chain_lo[k];
+        ck_hi = b.cm_chain_hi[k];
+        ck_t = b.cm_chain_type[k];
+        dv_t = b.cm_direct_type[v];
+        cv_t = b.cm_chain_type[v];
+        floor_k = b.cm_rank_floor[k];
+        vf = b.cm_rank_floor[v];
+        dother = b.cm_direct_other[k];
+        dk_lo = b.cm_direct_lo[k];
+        dk_hi = b.cm_direct_hi[k];
+        dk_t = b.cm_direct_type[k];
+    }
+    // ... and the eaten-by rows of pid o * 30 + lane that gain K: those in V's
+    // direct or chain set of observer o, or V itself
+    bool on[4];
+    uint64_t ea[4], eb[4];
+#pragma unroll
+    for (int o = 0; o < 4; ++o) {
+        const int t = o * 30 + lane;
+        const uint64_t lo = w.cmv[o][0] | w.cmv[o][2], hi = w.cmv[o][1] | w.cmv[o][3];
+        on[o] = lane < 30 && ((t < 64 ? (lo >> t) & 1ull : (hi >> (t - 64)) & 1ull) || (V_seat == o && t == V));
+        ea[o] = eb[o] = 0;
+        if (on[o]) {
+            ea[o] = b.cm_eaten_lo[OI(e, o, t)];
+            eb[o] = b.cm_eaten_hi[OI(e, o, t)];
+        }
+    }
     if (lane < 4) {
         const int o = lane;
-        const size_t k = OI(e, o, K), v = OI(e, o, V);
-        if (!eat && (b.cm_is_gongb[v] || (A_type == GONGB && o == V_seat))) b.cm_atk_gongb[k] = 1;
-        uint64_t lo = b.cm_chain_lo[k] | b.cm_direct_lo[v] | b.cm_chain_lo[v];
-        uint64_t hi = b.cm_chain_hi[k] | b.cm_direct_hi[v] | b.cm_chain_hi[v];
+        const uint64_t dv_lo = w.cmv[o][0], dv_hi = w.cmv[o][1], cv_lo = w.cmv[o][2], cv_hi = w.cmv[o][3];
+        if (!eat && (g_v || (A_type == GONGB && o == V_seat))) b.cm_atk_gongb[k] = 1;
+        uint64_t lo = ck_lo | dv_lo | cv_lo;
+        uint64_t hi = ck_hi | dv_hi | cv_hi;
         set_pid_bit(lo, hi, V);
         b.cm_chain_lo[k] = lo;
         b.cm_chain_hi[k] = hi;
-        uint16_t ctype = (uint16_t)(b.cm_chain_type[k] | b.cm_direct_type[v] | b.cm_chain_type[v]);
-        int floor_k = b.cm_rank_floor[k];
+        uint16_t ctype = (uint16_t)(ck_t | dv_t | cv_t);
         bool floor_up = false, not_g = false;
-        const int vf = b.cm_rank_floor[v], prop = vf + 1 < 9 ? vf + 1 : 9;
+        const int prop = vf + 1 < 9 ? vf + 1 : 9;
         if (vf > 0) {
             if (prop > floor_k) { floor_k = prop; floor_up = true; }
             not_g = true;
         }
         if (V_seat != o) {
-            const int c = b.cm_direct_other[k] + 1;
+            const int c = dother + 1;
             b.cm_direct_other[k] = (int16_t)(c < 32767 ? c : 32767);
         } else {
-            uint64_t dlo = b.cm_direct_lo[k], dhi = b.cm_direct_hi[k];
-            set_pid_bit(dlo, dhi, V);
-            b.cm_direct_lo[k] = dlo;
-            b.cm_direct_hi[k] = dhi;
+            set_pid_bit(dk_lo, dk_hi, V);
+            b.cm_direct_lo[k] = dk_lo;
+            b.cm_direct_hi[k] = dk_hi;
             if (v_idx >= 0) {
-                b.cm_direct_type[k] = (uint16_t)(b.cm_direct_type[k] | (1u << v_idx));
+                b.cm_direct_type[k] = (uint16_t)(dk_t | (1u << v_idx));
                 ctype = (uint16_t)(ctype | (1u << v_idx));
             }
             if (eat) {
@@ -518,21 +567,13 @@ __device__ void warp_cm_apply(const jq_batch &b, int e, int lane, bool eat, int 
         }
         if (not_g) b.cm_not_gongb[k] = 1;
     }
-    if (lane < 30) {
-        // reverse projection: observer-own pid o * 30 + lane gains K in its eaten-by set
-        // when V's direct or chain set (of observer o) holds it, or it is V itself
-        for (int o = 0; o < 4; ++o) {
-            const size_t v = OI(e, o, V);
-            const int t = o * 30 + lane;
-            const uint64_t lo = b.cm_direct_lo[v] | b.cm_chain_lo[v], hi = b.cm_direct_hi[v] | b.cm_chain_hi[v];
-            const bool on = (t < 64 ? (lo >> t) & 1ull : (hi >> (t - 64)) & 1ull) || (V_seat == o && t == V);
-            if (on) {
-                const size_t tt = OI(e, o, t);
-                uint64_t a = b.cm_eaten_lo[tt], c = b.cm_eaten_hi[tt];
-                set_pid_bit(a, c, K);
-                b.cm_eaten_lo[tt] = a;
-                b.cm_eaten_hi[tt] = c;
-            }
+#pragma unroll
+    for (int o = 0; o < 4; ++o) {
+        if (on[o]) {
+            const size_t tt = OI(e, o, o * 30 + lane);
+            set_pid_bit(ea[o], eb[o], K);
+            b.cm_eaten_lo[tt] = ea[o];
+            b.cm_eaten_hi[tt] = eb[o];
         }
     }
     __syncwarp();
@@ -561,10 +602,12 @@ __device__ __forceinline__ uint8_t initial_code(const Topo &T, const WEnv &w, in
     return BC_UNIFORM;
 }
 
-__device__ void warp_belief_init(const jq_batch &b, const Topo &T, const WEnv &w, int e, int lane, int mode) {
+__device__ void warp_belief_init(const jq_batch &b, const Topo &T, WEnv &w, int e, int lane, int mode) {
     for (int k = lane; k < 4 * NP; k += 32) {
         int o = k / NP, p = k - o * NP;
-        b.bel_code[OI(e, o, p)] = initial_code(T, w, o, p, mode);
+        const uint8_t c = initial_code(T, w, o, p, mode);
+        b.bel_code[OI(e, o, p)] = c;
+        w.bel[k] = c;
     }
     const int16_t counts[12] = {1, 3, 2, 1, 1, 2, 2, 2, 2, 3, 3, 3};
     for (int k = lane; k < 16 * 12; k += 32) {
@@ -589,18 +632,21 @@ __device__ __forceinline__ void rem_untrack(const jq_batch &b, int e, int o, int
 }
 
 // Lane o (0..3) applies R3, R5/R7, R4/R6, R1 and R9 for observer o; then the
-// whole warp runs the I5 sweep.
-__device__ void warp_belief_update(const jq_batch &b, const Topo &T, const WEnv &w, int e, int lane,
+// whole warp runs the I5 sweep.  The codes are the shared-memory copy
+// warp_load took; chunks the rules change are written back.
+__device__ void warp_belief_update(const jq_batch &b, const Topo &T, WEnv &w, int e, int lane,
                                    const StepCtx &x, int mode, const int *died) {
+    bool touched = false;  // R-rules rewrote a code of this lane's observer
     if (lane < 4) {
         int o = lane;
-        uint8_t *code = b.bel_code + OI(e, o, 0);
+        uint8_t *code = w.bel + o * NP;
         int a_bel = code[x.A];
         int d_bel = x.D >= 0 ? code[x.D] : BC_NONE;
         if (x.fr_src) rem_dec(b, e, o, x.acting, SILING - 2);
         if (x.fr_dst) rem_dec(b, e, o, x.D_seat, SILING - 2);
         if (x.ev == EV_EAT && x.D >= 0 && x.D_type == DILEI && a_bel != BC_NONE && !bc_onehot(a_bel)) {
             code[x.A] = (uint8_t)(GONGB - 1);
+            touched = true;
             a_bel = code[x.A];
             rem_dec(b, e, o, x.acting, GONGB - 2);
         }
@@ -608,7 +654,10 @@ __device__ void warp_belief_update(const jq_batch &b, const Topo &T, const WEnv 
             if (x.D_seat >= 0 && x.D_seat < 4) rem_untrack(b, e, o, x.D_seat);
         } else if (x.ev == EV_EAT && x.other_pid >= 0) {
             int op = x.other_pid;
-            if (code[op] != BC_NONE && !bc_onehot(code[op])) code[op] = (uint8_t)(JUNQI - 1);
+            if (code[op] != BC_NONE && !bc_onehot(code[op])) {
+                code[op] = (uint8_t)(JUNQI - 1);
+                touched = true;
+            }
         }
         a_bel = code[x.A];
         if (x.ev == EV_EAT) {
@@ -622,14 +671,33 @@ __device__ void warp_belief_update(const jq_batch &b, const Topo &T, const WEnv 
         for (int s = 0; s < 4; ++s)
             if (died[s]) rem_untrack(b, e, o, s);
     }
+    const bool any_touched = __any_sync(FULL, touched);
+    // alive bits of pids 0..119 (bit p of word p >> 5)
+    uint32_t am[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) am[i] = __ballot_sync(FULL, lane + 32 * i < NP && w.alive[lane + 32 * i]);
     __syncwarp();
     // I5 sweep over the env's 4 x 120 codes, 16 per lane (rows are 480 bytes,
-    // 16-byte aligned: the host checks the base)
+    // 16-byte aligned: the host checks the base).  I5 rewrites a code exactly
+    // when (code != NONE) differs from alive, so a chunk whose nonzero-byte
+    // mask equals its pids' alive bits is left as it is.
     if (lane < 4 * NP / 16) {
-        uint4 *row = reinterpret_cast<uint4 *>(b.bel_code + OI(e, 0, 0)) + lane;
-        uint4 v = *row;
+        uint4 *srow = reinterpret_cast<uint4 *>(w.bel) + lane;
+        uint4 v = *srow;
         uint32_t wv[4] = {v.x, v.y, v.z, v.w};
-        bool changed = false;
+        uint32_t nz = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)  // byte b of word j nonzero -> bit 4 j + b
+            nz |= ((((__vcmpne4(wv[j], 0u) & 0x01010101u) * 0x10204080u) >> 28) << (4 * j));
+        // alive bits of the chunk's pids p0 .. p0 + 15, wrapping at 120 into the next observer
+        const int p0 = (lane * 16) % NP;
+        uint32_t al = __funnelshift_r(am[p0 >> 5], (p0 >> 5) + 1 < 4 ? am[(p0 >> 5) + 1] : 0u, p0 & 31) & 0xffffu;
+        if (p0 + 16 > NP) {
+            const int n1 = NP - p0;
+            al = (al & ((1u << n1) - 1u)) | ((am[0] & ((1u << (16 - n1)) - 1u)) << n1);
+        }
+        bool changed = any_touched;
+        if (nz != al)
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
             const int k = lane * 16 + i, o = k >= 3 * NP ? 3 : k >= 2 * NP ? 2 : k >= NP ? 1 : 0, p = k - o * NP;
@@ -643,7 +711,11 @@ __device__ void warp_belief_update(const jq_batch &b, const Topo &T, const WEnv 
                 wv[i >> 2] = (wv[i >> 2] & ~(0xFFu << ((i & 3) * 8))) | (nc << ((i & 3) * 8));
             }
         }
-        if (changed) *row = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+        if (changed) {
+            const uint4 nv = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+            *srow = nv;
+            reinterpret_cast<uint4 *>(b.bel_code + OI(e, 0, 0))[lane] = nv;
+        }
     }
     __syncwarp();
 }
@@ -907,7 +979,7 @@ __device__ bool warp_step(const jq_batch &b, const Topo &T, WEnv &w, int e, int 
         }
     }
     __syncwarp();
-    if (x.cm) warp_cm_apply(b, e, lane, x.cm == 1, x.A, x.D, x.A_seat, x.D_seat, x.A_type, x.D_type, x.new_mc);
+    if (x.cm) warp_cm_apply(b, w, e, lane, x.cm == 1, x.A, x.D, x.A_seat, x.D_seat, x.A_type, x.D_type, x.new_mc);
     if (x.need_surrender) {
         int64_t d = warp_surrender(b, T, w, e, lane, x.D_seat, x.new_mc);
         if (lane == 0) zob ^= d;
