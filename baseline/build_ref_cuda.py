@@ -11,11 +11,11 @@ the reference's ``GpuRollout`` per-ply chain with it.
 
 Run where the reference checkout exists::
 
-    python baseline/build_ref_cuda.py [<reference checkout>]
+    python baseline/build_ref_cuda.py <reference checkout>
 
 Nothing is written into the reference checkout: sources are compiled from
 a copy under a temporary directory.  The one source change the build needs
-on CUDA 12.9 (found by the survey of this path) is dropping the
+on CUDA 12.9 is dropping the
 ``#undef __noinline__`` block of ``rollout_history.cu``, which otherwise
 breaks the CUDA headers included after it; it is made in the copy.
 """
@@ -41,7 +41,9 @@ def run(cmd, **kw):
 
 
 def main() -> None:
-    ref = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference").resolve()
+    if len(sys.argv) != 2:
+        raise SystemExit("usage: python baseline/build_ref_cuda.py <reference checkout>")
+    ref = Path(sys.argv[1]).resolve()
     import pybind11
     OUT.mkdir(parents=True, exist_ok=True)
     with tempfile.TemporaryDirectory() as tmp:

@@ -8,7 +8,7 @@ would add (it routes ``import junqi_cuda`` to ``junqi_b200.junqi_cuda``).
 The reference's compiled extension is not copied, so every test there runs
 on this library's kernels.  Run on a GPU box from the repository root::
 
-    python baseline/stage_ref_tests.py [<reference checkout>]      # where the checkout exists
+    python baseline/stage_ref_tests.py <reference checkout>      # where the checkout exists
     cd baseline/_ref/dropin && python -m pytest -q -p no:cacheprovider tests
 
 Nothing is written into the reference checkout.
@@ -39,7 +39,9 @@ sys.modules[__name__] = _impl
 
 
 def main() -> None:
-    ref = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference").resolve()
+    if len(sys.argv) != 2:
+        raise SystemExit("usage: python baseline/stage_ref_tests.py <reference checkout>")
+    ref = Path(sys.argv[1]).resolve()
     if OUT.exists():
         shutil.rmtree(OUT)
     OUT.mkdir(parents=True)
