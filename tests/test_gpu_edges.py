@@ -10,6 +10,8 @@
   game) leave the env untouched and report valid = 0.
 * Explicit observer lists of any order give the oracle's observation of
   each listed seat.
+* Belief codes uploaded out of step with the board are repaired by the
+  next ply's sweep as the oracle repairs them.
 """
 from __future__ import annotations
 
@@ -143,3 +145,47 @@ def test_episode_cap_draws_like_the_oracle(rules):
             orc.reset_env(int(e), pool[L.jq_pool_index(17, t, int(e), pool.shape[0])])
         _compare_state(env, orc, t)
     assert draws >= 24
+
+
+def test_belief_sweep_repairs_codes_written_by_the_host():
+    """Belief codes that contradict the board -- an alive piece with no code,
+    a dead piece holding one, as a caller's state upload can leave them --
+    are repaired by the next ply's I5 sweep exactly as the oracle repairs
+    them, in every 16-code chunk (the sweep skips only chunks whose codes
+    already agree with the alive bits)."""
+    n, seed = 32, 29
+    env, orc, pool = _pair(n, seed, late=True)
+    st = env.state()
+    codes = np.asarray(st["bel_code"]).reshape(n, 4, 120).copy()
+    alive = np.asarray(st["alive"]).reshape(n, 120).astype(bool)
+    rng = np.random.default_rng(seed)
+    planted = 0
+    for e in range(n):
+        live, dead = np.nonzero(alive[e])[0], np.nonzero(~alive[e])[0]
+        for o in range(4):
+            if len(live):
+                codes[e, o, rng.choice(live, size=min(3, len(live)), replace=False)] = 0
+                planted += 1
+            if len(dead):
+                codes[e, o, rng.choice(dead, size=min(2, len(dead)), replace=False)] = 14
+                planted += 1
+    assert planted > 0
+    env.batch.load({"bel_code": codes})
+    O.load_state(orc, {"bel_code": codes}, init_beliefs=False)
+    L = N.lib()
+    stepped = np.zeros(n, dtype=bool)
+    for t in range(1, 4):
+        acts = env.sample_uniform(seed, t)
+        a = acts.cpu().numpy().copy()
+        out = env.ply(acts, seed=seed, ply=t)
+        r = orc.step(a)
+        assert np.array_equal(out["valid"].cpu().numpy().astype(r["valid"].dtype), r["valid"]), t
+        stepped |= r["valid"].astype(bool)
+        for e in np.nonzero(r["terminated"])[0]:
+            orc.reset_env(int(e), pool[L.jq_pool_index(seed, t, int(e), pool.shape[0])])
+        _compare_state(env, orc, t)
+    assert stepped.sum() >= n // 2
+    fixed = np.asarray(env.state()["bel_code"]).reshape(n, 4, 120)[stepped]
+    alive = np.asarray(env.state()["alive"]).reshape(n, 120).astype(bool)[stepped]
+    assert ((fixed != 0) == alive[:, None, :]).all()
+    _compare_obs(env, orc, 3, seats=1)
