@@ -16,7 +16,7 @@
 #include <stddef.h>
 #include <stdint.h>
 
-#define JQ_ABI_VERSION 5
+#define JQ_ABI_VERSION 6
 
 #define JQ_NUM_PIECES 120
 #define JQ_NUM_CELLS 289
@@ -248,6 +248,37 @@ int jq_history_snapshot(const jq_batch *b, const int8_t *d_seats, void *d_histor
  * legal actions, canonical mask and observation exactly as they were. */
 int jq_history_restore(const void *d_history, int64_t num_records, const int64_t *d_indices,
                        const jq_batch *scratch, int8_t *d_observers, void *stream);
+
+/* Per-cell float beliefs of the reference's GPU rollout (belief.cu), kept
+ * by the caller in d_beliefs, a 16-byte aligned (N, 4, 12, 289) float32
+ * array [env][observer][type][world flat cell] -- the input
+ * jq_observe_beliefs reads.  These follow the reference GPU kernels' own
+ * rules; the beliefs the step maintains itself (jq_batch.bel_code) follow
+ * the CPU BeliefTensor.
+ *
+ * jq_cell_beliefs_init: clear the envs with d_env_mask[e] != 0 (NULL: all)
+ * and seed every alive on-board piece: one-hot for its owner, the row of
+ * its slot in d_prior (30 x 12 float32, device) for the other observers.
+ * Replaces init_all_beliefs / init_beliefs_for_reset_envs
+ * (bindings.cpp:1252-1270, belief.cu:172-248, 599-643). */
+int jq_cell_beliefs_init(const jq_batch *b, const uint8_t *d_env_mask, const float *d_prior, float *d_beliefs,
+                         void *stream);
+
+/* seat_dead (N x 4) and terminated (N) as they are now, into caller buffers
+ * (either may be NULL).  Replaces snapshot_pre_step_flags
+ * (bindings.cpp:1272-1278, belief.cu:570-584, 645-671). */
+int jq_cell_beliefs_snapshot(const jq_batch *b, uint8_t *d_prev_dead, uint8_t *d_prev_terminated, void *stream);
+
+/* Update after a step, on the batch's post-step state: the step's event,
+ * flag_captured and world action per env (jq_step_out fields), the
+ * seat_dead snapshot d_prev_dead, and d_strongholds (4 x 2 int16, device:
+ * each seat's two stronghold flat cells).  Envs now terminated, or whose
+ * event is 0, are left as they are.  Rules R5/R7, R1, R6, R4 and the I5
+ * sweep.  Replaces update_beliefs_after_step (bindings.cpp:1280-1300,
+ * belief.cu:255-565, 673-706). */
+int jq_cell_beliefs_update(const jq_batch *b, const int8_t *d_event, const uint8_t *d_flag_captured,
+                           const int32_t *d_world_actions, const uint8_t *d_prev_dead, const int16_t *d_strongholds,
+                           float *d_beliefs, void *stream);
 
 /* Legal actions for `d_seats` (NULL: each env's turn), ascending and
  * de-duplicated per env (BatchedGameState.legal_action_ids_batch,

@@ -85,6 +85,9 @@ SIGNATURES = {
     "jq_csr_noalloc": (ctypes.c_int, [_i32, _vp, _vp, _i32, _vp, _vp, _vp]),
     "jq_observe": (ctypes.c_int, [_PB, _vp, _i32, _i32, _vp, _vp, _vp]),
     "jq_observe_beliefs": (ctypes.c_int, [_PB, _vp, _i32, _i32, _vp, _vp, _vp, _vp]),
+    "jq_cell_beliefs_init": (ctypes.c_int, [_PB, _vp, _vp, _vp, _vp]),
+    "jq_cell_beliefs_snapshot": (ctypes.c_int, [_PB, _vp, _vp, _vp]),
+    "jq_cell_beliefs_update": (ctypes.c_int, [_PB, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "jq_sample_uniform": (ctypes.c_int, [_i32, _vp, _vp, _i32, _u64, _u64, _vp, _vp]),
     "jq_sample_softmax": (ctypes.c_int, [_PB, _vp, _vp, _i32, _u64, _u64, _vp, _vp, _vp]),
 }

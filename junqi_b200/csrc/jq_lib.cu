@@ -11,6 +11,7 @@
 #include <atomic>
 #include <mutex>
 
+#include "jq_cellbel.cuh"
 #include "jq_hist.cuh"
 #include "jq_obs.cuh"
 #include "jq_ply.cuh"
@@ -578,6 +579,52 @@ int jq_history_restore(const void *d_history, int64_t num_records, const int64_t
         *scratch, static_cast<const HistRec *>(d_history), (long long)num_records,
         reinterpret_cast<const long long *>(d_indices), d_observers);
     CU(cudaGetLastError());
+    return JQ_OK;
+}
+
+static int cellbel_common(const jq_batch *b, const float *d_beliefs) {
+    int rc = check_batch(b);
+    if (rc) return rc;
+    DeviceState *st;
+    rc = current_dev(st);
+    if (rc) return rc;
+    if (!st->topo) return fail(JQ_ERR_NOT_READY, "jq_init was not called on this device");
+    if (!d_beliefs || ((uintptr_t)d_beliefs & 15))
+        return fail(JQ_ERR_ARG, "beliefs must be a 16-byte aligned (N, 4, 12, 289) float32 array");
+    return JQ_OK;
+}
+
+int jq_cell_beliefs_init(const jq_batch *b, const uint8_t *d_env_mask, const float *d_prior, float *d_beliefs,
+                         void *stream) {
+    int rc = cellbel_common(b, d_beliefs);
+    if (rc) return rc;
+    if (!d_prior || ((uintptr_t)d_prior & 3)) return fail(JQ_ERR_ARG, "prior must be a 30 x 12 float32 array");
+    CU(launch_pdl(cellbel_init_kernel, (unsigned)b->n, CB_INIT_THREADS, 0, (cudaStream_t)stream, *b, d_env_mask,
+                  d_prior, d_beliefs));
+    return JQ_OK;
+}
+
+int jq_cell_beliefs_snapshot(const jq_batch *b, uint8_t *d_prev_dead, uint8_t *d_prev_terminated, void *stream) {
+    int rc = check_batch(b);
+    if (rc) return rc;
+    if (!d_prev_dead && !d_prev_terminated) return fail(JQ_ERR_ARG, "no snapshot output given");
+    CU(launch_pdl(cellbel_snapshot_kernel, (unsigned)((b->n + 255) / 256), 256, 0, (cudaStream_t)stream, *b,
+                  d_prev_dead, d_prev_terminated));
+    return JQ_OK;
+}
+
+int jq_cell_beliefs_update(const jq_batch *b, const int8_t *d_event, const uint8_t *d_flag_captured,
+                           const int32_t *d_world_actions, const uint8_t *d_prev_dead, const int16_t *d_strongholds,
+                           float *d_beliefs, void *stream) {
+    int rc = cellbel_common(b, d_beliefs);
+    if (rc) return rc;
+    if (!d_event || !d_flag_captured || !d_world_actions || !d_prev_dead || !d_strongholds)
+        return fail(JQ_ERR_ARG, "step results, seat_dead snapshot and stronghold table are required");
+    if (((uintptr_t)d_world_actions & 3) || ((uintptr_t)d_strongholds & 1))
+        return fail(JQ_ERR_ARG, "world actions / strongholds misaligned");
+    CU(launch_pdl(cellbel_update_kernel, (unsigned)((b->n + CB_WARPS - 1) / CB_WARPS), CB_WARPS * 32, 0,
+                  (cudaStream_t)stream, *b, d_event, d_flag_captured, d_world_actions, d_prev_dead, d_strongholds,
+                  d_beliefs));
     return JQ_OK;
 }
 

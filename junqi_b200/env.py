@@ -182,6 +182,51 @@ class JunqiEnvB200:
                                                _stream_ptr()), "jq_observe_beliefs")
         return self.spatial[: self.n * s], self.global_[: self.n * s]
 
+    # -- per-cell float beliefs of the reference GPU rollout (belief.cu) --------
+    def cell_beliefs_init(self, beliefs: torch.Tensor, prior: torch.Tensor,
+                          env_mask: torch.Tensor | None = None) -> torch.Tensor:
+        """Seed ``beliefs`` ((N, 4, 12, 289) float32 on this device) for the envs
+        with env_mask[e] != 0 (default all): one-hot rows for each observer's own
+        pieces, the slot's row of ``prior`` (30 x 12) for every other piece."""
+        self._check_cell_beliefs(beliefs)
+        pr = prior.to(device=self.device, dtype=torch.float32).contiguous()
+        if pr.numel() != 360:
+            raise ValueError("prior must hold 30 x 12 floats")
+        m = None if env_mask is None else env_mask.to(device=self.device, dtype=torch.uint8).contiguous()
+        N.check(N.lib().jq_cell_beliefs_init(ctypes.byref(self.batch.struct), self._ptr(m), pr.data_ptr(),
+                                             beliefs.data_ptr(), _stream_ptr()), "jq_cell_beliefs_init")
+        return beliefs
+
+    def cell_beliefs_snapshot(self) -> tuple[torch.Tensor, torch.Tensor]:
+        """(seat_dead (N, 4), terminated (N,)) as uint8 copies, taken before a step."""
+        dead = torch.empty((self.n, 4), dtype=torch.uint8, device=self.device)
+        term = torch.empty(self.n, dtype=torch.uint8, device=self.device)
+        N.check(N.lib().jq_cell_beliefs_snapshot(ctypes.byref(self.batch.struct), dead.data_ptr(), term.data_ptr(),
+                                                 _stream_ptr()), "jq_cell_beliefs_snapshot")
+        return dead, term
+
+    def cell_beliefs_update(self, beliefs: torch.Tensor, world_actions: torch.Tensor, prev_dead: torch.Tensor,
+                            strongholds: torch.Tensor) -> torch.Tensor:
+        """Apply the last step (its event and flag capture in ``self.out``) to
+        ``beliefs``; ``prev_dead`` from cell_beliefs_snapshot before the step,
+        ``strongholds`` (4 x 2) each seat's stronghold flat cells."""
+        self._check_cell_beliefs(beliefs)
+        wa = world_actions.to(device=self.device, dtype=torch.int32).contiguous()
+        pd = prev_dead.to(device=self.device, dtype=torch.uint8).contiguous()
+        sh = strongholds.to(device=self.device, dtype=torch.int16).contiguous()
+        if wa.numel() != self.n or pd.numel() != 4 * self.n or sh.numel() != 8:
+            raise ValueError("world_actions (N,), prev_dead (N, 4) and strongholds (4, 2) expected")
+        N.check(N.lib().jq_cell_beliefs_update(ctypes.byref(self.batch.struct), self.out["event"].data_ptr(),
+                                               self.out["flag_captured"].data_ptr(), wa.data_ptr(), pd.data_ptr(),
+                                               sh.data_ptr(), beliefs.data_ptr(), _stream_ptr()),
+                "jq_cell_beliefs_update")
+        return beliefs
+
+    def _check_cell_beliefs(self, beliefs: torch.Tensor) -> None:
+        if (beliefs.dtype != torch.float32 or tuple(beliefs.shape) != (self.n, 4, 12, 289)
+                or not beliefs.is_contiguous() or beliefs.device != torch.device(self.device)):
+            raise ValueError(f"beliefs must be a contiguous ({self.n}, 4, 12, 289) float32 tensor on {self.device}")
+
     def sample_uniform(self, seed: int, ply: int) -> torch.Tensor:
         N.check(N.lib().jq_sample_uniform(self.n, self.counts.data_ptr(), self.ids.data_ptr(), self.cap, seed, ply,
                                           self.actions.data_ptr(), _stream_ptr()), "jq_sample_uniform")

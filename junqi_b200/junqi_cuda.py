@@ -120,16 +120,41 @@ def upload_setup_pool(piece_types) -> None:
 
 
 def upload_belief_prior_table(prior) -> None:
+    global _cell_prior
     p = np.ascontiguousarray(prior, dtype=np.float32).reshape(-1)
     if p.size != 360:
         raise RuntimeError("upload_belief_prior_table: expected 360 floats")
+    _cell_prior = torch.from_numpy(p.copy()).to(f"cuda:{_device}")
     N.check(N.lib().jq_upload_obs_tables(p.ctypes.data, tables.uniform12().ctypes.data,
                                          tables.recency_lut().ctypes.data), "jq_upload_obs_tables")
 
 
 def upload_seat_strongholds(strongholds) -> None:
+    global _cell_strongholds
     if np.asarray(strongholds).size != 8:
         raise RuntimeError("upload_seat_strongholds: expected 8 entries")
+    _cell_strongholds = torch.from_numpy(np.ascontiguousarray(strongholds, dtype=np.int16).reshape(8).copy()).to(
+        f"cuda:{_device}")
+
+
+# Per-cell float beliefs of the reference's GPU rollout (belief.cu), opt-in.
+# By default the belief calls below are no-ops and observations use the
+# beliefs the step maintains with the CPU BeliefTensor rules; after
+# use_reference_gpu_beliefs(True) they run the reference GPU kernels' rules
+# (jq_cell_beliefs_*) on a resident (N, 4, 12, 289) tensor that
+# build_observation_batch_resident then reads, as the reference does.
+_cell_mode = False
+_cell_prior: torch.Tensor | None = None
+_cell_strongholds: torch.Tensor | None = None
+_cell_prev_dead: torch.Tensor | None = None
+_cell_prev_term: torch.Tensor | None = None
+
+
+def use_reference_gpu_beliefs(enabled: bool = True) -> None:
+    """Select the reference GPU rollout's per-cell belief rules for the
+    init / snapshot / update belief calls (default: off)."""
+    global _cell_mode
+    _cell_mode = bool(enabled)
 
 
 _beliefs: torch.Tensor | None = None  # uploaded per-cell beliefs (N, 4, 12, 289) float32
@@ -157,10 +182,11 @@ def upload_observer_seats(num_envs: int, observer_seats) -> None:
 
 
 def gpu_scratch_reset() -> None:
-    """Forget uploaded beliefs and observer seats."""
-    global _beliefs, _observer_seats
+    """Forget uploaded beliefs, observer seats and belief snapshots."""
+    global _beliefs, _observer_seats, _cell_prev_dead, _cell_prev_term
     _beliefs = None
     _observer_seats = None
+    _cell_prev_dead = _cell_prev_term = None
 
 
 def device_synchronize() -> None:
@@ -408,23 +434,69 @@ def record_move_history(state, d_world_actions_ptr, d_valid_ptr) -> None:
     """The move history is recorded inside the step."""
 
 
+def _cell_ready(state, what: str) -> None:
+    if _cell_prior is None or _cell_strongholds is None:
+        raise RuntimeError(f"{what}: call upload_belief_prior_table and upload_seat_strongholds first")
+    if _beliefs is None or _beliefs.shape[0] != state.num_envs:
+        raise RuntimeError(f"{what}: call init_all_beliefs first")
+
+
 def snapshot_pre_step_flags(state) -> None:
-    """Not needed: belief updates happen inside the step."""
+    """bindings.cpp:1272-1278.  Default mode: nothing to do (the step updates
+    its own beliefs); reference GPU beliefs: seat_dead and terminated now."""
+    global _cell_prev_dead, _cell_prev_term
+    if not _cell_mode:
+        return
+    n = state.num_envs
+    if _cell_prev_dead is None or _cell_prev_dead.shape[0] != n:
+        _cell_prev_dead = torch.zeros((n, 4), dtype=torch.uint8, device=f"cuda:{_device}")
+        _cell_prev_term = torch.zeros(n, dtype=torch.uint8, device=f"cuda:{_device}")
+    N.check(N.lib().jq_cell_beliefs_snapshot(ctypes.byref(state.b.struct), _cell_prev_dead.data_ptr(),
+                                             _cell_prev_term.data_ptr(), _stream()), "jq_cell_beliefs_snapshot")
 
 
 def update_beliefs_after_step(state, d_event_ptr=0, d_flag_captured_ptr=0, d_world_actions_ptr=0) -> None:
-    """Beliefs are updated inside the step with the BeliefTensor rules."""
+    """bindings.cpp:1280-1300.  Default mode: beliefs were updated inside the
+    step with the BeliefTensor rules; reference GPU beliefs: belief.cu's
+    update from the step's event / flag capture / world action."""
+    if not _cell_mode:
+        return
+    _cell_ready(state, "update_beliefs_after_step")
+    if _cell_prev_dead is None or _cell_prev_dead.shape[0] != state.num_envs:
+        raise RuntimeError("update_beliefs_after_step: call snapshot_pre_step_flags first")
+    N.check(N.lib().jq_cell_beliefs_update(ctypes.byref(state.b.struct), int(d_event_ptr), int(d_flag_captured_ptr),
+                                           int(d_world_actions_ptr), _cell_prev_dead.data_ptr(),
+                                           _cell_strongholds.data_ptr(), _beliefs.data_ptr(), _stream()),
+            "jq_cell_beliefs_update")
 
 
 def init_beliefs_for_reset_envs(state) -> None:
-    """Resets initialise beliefs themselves."""
+    """bindings.cpp:1252-1260.  Default mode: resets initialise beliefs
+    themselves; reference GPU beliefs: re-seed the envs the last snapshot
+    saw terminated."""
+    if not _cell_mode:
+        return
+    _cell_ready(state, "init_beliefs_for_reset_envs")
+    if _cell_prev_term is None or _cell_prev_term.shape[0] != state.num_envs:
+        raise RuntimeError("init_beliefs_for_reset_envs: call snapshot_pre_step_flags first")
+    N.check(N.lib().jq_cell_beliefs_init(ctypes.byref(state.b.struct), _cell_prev_term.data_ptr(),
+                                         _cell_prior.data_ptr(), _beliefs.data_ptr(), _stream()),
+            "jq_cell_beliefs_init")
 
 
 def init_all_beliefs(state: DeviceGameStateBatch) -> None:
-    """Prior beliefs for every env; observations use the library's beliefs again."""
+    """bindings.cpp:1262-1270.  Default mode: prior beliefs for every env, and
+    observations use the library's beliefs again; reference GPU beliefs: a
+    resident per-cell tensor seeded for every env."""
     global _beliefs
     _beliefs = None
     N.check(N.lib().jq_init_beliefs(ctypes.byref(state.b.struct), state.show_mode, _stream()), "jq_init_beliefs")
+    if _cell_mode:
+        if _cell_prior is None:
+            raise RuntimeError("init_all_beliefs: call upload_belief_prior_table first")
+        _beliefs = torch.zeros((state.num_envs, 4, 12, 289), dtype=torch.float32, device=f"cuda:{_device}")
+        N.check(N.lib().jq_cell_beliefs_init(ctypes.byref(state.b.struct), None, _cell_prior.data_ptr(),
+                                             _beliefs.data_ptr(), _stream()), "jq_cell_beliefs_init")
 
 
 def reset_terminated_envs(state: DeviceGameStateBatch, seed: int) -> None:

@@ -8,6 +8,7 @@
  */
 #include "jq_oracle.h"
 
+#include <math.h>
 #include <stdlib.h>
 #include <string.h>
 #ifdef _OPENMP
@@ -1528,5 +1529,134 @@ int jqo_obs_batch(const jqo_batch *b, const int8_t *observers, int mode, float *
 #pragma omp parallel for schedule(dynamic, 8) num_threads(nthreads > 0 ? nthreads : 1)
     for (int e = 0; e < b->n; ++e)
         jqo_obs(b, e, observers[e], mode, sp + (size_t)e * JQO_OBS_CH * NC, gl + (size_t)e * JQO_OBS_GLOBAL);
+    return 0;
+}
+
+/* ------------------------------------------------------------------------
+ * Per-cell float beliefs of the reference GPU rollout (belief.cu).  Values
+ * are copied, set to 0 / 1, to prior rows or to 1/12; the tests on them use
+ * the reference's float forms (running float sum, fmaxf chain).
+ * ------------------------------------------------------------------------ */
+#define CB_T 12
+static float *cb_at(float *bel, int env, int o, int cell) {
+    return bel + ((size_t)env * 4 + o) * CB_T * NC + cell; /* type t at [t * NC] */
+}
+static void cb_read(float *bel, int env, int o, int cell, float *v) {
+    const float *p = cb_at(bel, env, o, cell);
+    for (int t = 0; t < CB_T; ++t) v[t] = p[t * NC];
+}
+static void cb_write(float *bel, int env, int o, int cell, const float *v) {
+    float *p = cb_at(bel, env, o, cell);
+    for (int t = 0; t < CB_T; ++t) p[t * NC] = v[t];
+}
+static void cb_zero(float *bel, int env, int o, int cell) {
+    float *p = cb_at(bel, env, o, cell);
+    for (int t = 0; t < CB_T; ++t) p[t * NC] = 0.f;
+}
+static int cb_one_hot(const float *v) { /* belief.cu:71-76 */
+    float mx = 0.f;
+    for (int t = 0; t < CB_T; ++t) mx = fmaxf(mx, v[t]);
+    return mx > (1.0f - 1e-6f);
+}
+static int cb_argmax(const float *v) { /* belief.cu:79-90 */
+    int best = 0;
+    float bv = v[0];
+    for (int t = 1; t < CB_T; ++t)
+        if (v[t] > bv) { bv = v[t]; best = t; }
+    return best;
+}
+static int cb_is_zero(const float *v) { /* belief.cu:110-115 */
+    float s = 0.f;
+    for (int t = 0; t < CB_T; ++t) s += v[t];
+    return s < 1e-8f;
+}
+static void cb_set_one_hot(float *v, int ti) {
+    for (int t = 0; t < CB_T; ++t) v[t] = t == ti ? 1.f : 0.f;
+}
+
+int jqo_cellbel_init(const jqo_batch *b, int env, const float *prior, float *bel) {
+    memset(cb_at(bel, env, 0, 0), 0, sizeof(float) * 4 * CB_T * NC);
+    for (int p = 0; p < NP; ++p) { /* belief.cu:208-247 */
+        const size_t q = (size_t)env * NP + p;
+        if (!b->alive[q]) continue;
+        const int seat = b->piece_seat[q], type = b->piece_type[q], px = b->pos_x[q], py = b->pos_y[q];
+        if (px < 0 || py < 0 || px > 16 || py > 16) continue;
+        const int cell = py * 17 + px, ti = (type >= 2 && type <= 13) ? type - 2 : -1;
+        if (ti < 0) continue;
+        for (int o = 0; o < 4; ++o) {
+            float *c = cb_at(bel, env, o, cell);
+            if (o == seat) c[ti * NC] = 1.f;
+            else
+                for (int t = 0; t < CB_T; ++t) c[t * NC] = prior[(p % 30) * CB_T + t];
+        }
+    }
+    return 0;
+}
+
+int jqo_cellbel_update(const jqo_batch *b, int env, int event, int flag_cap, int32_t act, const uint8_t *prev_dead,
+                       const int16_t *sh, float *bel) {
+    build_topology();
+    if (b->terminated[env] || event == 0) return 0; /* belief.cu:275-281 */
+    if (act < 0 || act >= NC * NC) return 0;
+    const int src = act / NC, dst = act % NC;
+    const int16_t *cpid = b->cell_pid + (size_t)env * NC;
+    const uint8_t *sdead = b->seat_dead + (size_t)env * 4;
+    int surrendered = -1; /* belief.cu:363-375: the first newly dead seat of a flag capture */
+    if (flag_cap)
+        for (int s = 0; s < 4; ++s)
+            if (sdead[s] && !prev_dead[s]) { surrendered = s; break; }
+    int owner = -1, other = -1; /* belief.cu:380-402 */
+    if (T_sh[dst])
+        for (int s = 0; s < 4; ++s) {
+            if (sh[2 * s] == dst) { owner = s; other = sh[2 * s + 1]; break; }
+            if (sh[2 * s + 1] == dst) { owner = s; other = sh[2 * s]; break; }
+        }
+    for (int o = 0; o < 4; ++o) {
+        float vs[CB_T], vd[CB_T];
+        cb_read(bel, env, o, src, vs);
+        cb_read(bel, env, o, dst, vd);
+        /* R5/R7 (belief.cu:425-440): eating a known mine makes the attacker an engineer */
+        if (event == 2 && cb_one_hot(vd) && cb_argmax(vd) == 1 && !cb_one_hot(vs)) cb_set_one_hot(vs, 11);
+        /* R1 migration (belief.cu:444-469) */
+        if (event == 1 || event == 2) {
+            cb_write(bel, env, o, dst, vs);
+            cb_zero(bel, env, o, src);
+        } else if (event == 4) {
+            cb_zero(bel, env, o, src);
+        } else if (event == 3) {
+            cb_zero(bel, env, o, src);
+            cb_zero(bel, env, o, dst);
+        }
+        /* R6 (belief.cu:473-486): an eaten stronghold piece that is not the
+         * flag puts the flag on the seat's other stronghold */
+        if (event == 2 && T_sh[dst] && !flag_cap && owner >= 0 && other >= 0 && other < NC) {
+            float v[CB_T];
+            cb_read(bel, env, o, other, v);
+            if (!cb_is_zero(v) && !cb_one_hot(v)) {
+                cb_set_one_hot(v, 0);
+                cb_write(bel, env, o, other, v);
+            }
+        }
+        /* R4 (belief.cu:490-505): after a flag capture every empty cell is cleared */
+        if (flag_cap && surrendered >= 0)
+            for (int c = 0; c < NC; ++c)
+                if (cpid[c] < 0) cb_zero(bel, env, o, c);
+        /* I5 sweep (belief.cu:518-562) */
+        for (int c = 0; c < NC; ++c) {
+            const int p = cpid[c];
+            float v[CB_T];
+            cb_read(bel, env, o, c, v);
+            if (p < 0 || p >= NP || !b->alive[(size_t)env * NP + p]) {
+                if (!cb_is_zero(v)) cb_zero(bel, env, o, c);
+            } else if (cb_is_zero(v)) {
+                const int ps = b->piece_seat[(size_t)env * NP + p], pt = b->piece_type[(size_t)env * NP + p];
+                const int ti = (pt >= 2 && pt <= 13) ? pt - 2 : -1;
+                if ((o & 1) == (ps & 1) && ti >= 0) cb_set_one_hot(v, ti);
+                else
+                    for (int t = 0; t < CB_T; ++t) v[t] = 1.0f / (float)CB_T;
+                cb_write(bel, env, o, c, v);
+            }
+        }
+    }
     return 0;
 }

@@ -119,6 +119,17 @@ int jqo_obs_ext(const jqo_batch *b, int env, int observer, int show_mode, const 
                 float *global);
 int jqo_obs_ext_batch(const jqo_batch *b, const int8_t *observers, int show_mode, const float *bel,
                       float *spatial, float *global, int nthreads);
+/* Per-cell float beliefs of the reference's GPU rollout (belief.cu), in
+ * bel (N, 4, 12, 289) [env][observer][type][world cell]:
+ * jqo_cellbel_init -- belief_init_kernel (belief.cu:172-248) for one env,
+ * prior = the 30 x 12 per-slot table the caller uploads;
+ * jqo_cellbel_update -- belief_update_kernel (belief.cu:255-565) for one env
+ * on its post-step state, with the step's event / flag capture / world
+ * action, the seat_dead snapshot prev_dead (4) and the 4 x 2 stronghold
+ * cells of each seat. */
+int jqo_cellbel_init(const jqo_batch *b, int env, const float *prior, float *bel);
+int jqo_cellbel_update(const jqo_batch *b, int env, int event, int flag_captured, int32_t world_action,
+                       const uint8_t *prev_dead, const int16_t *strongholds, float *bel);
 #ifdef __cplusplus
 }
 #endif

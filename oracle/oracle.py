@@ -337,6 +337,30 @@ class OracleBatch:
                                 self.threads)
         return sp, gl
 
+    def cellbel_init(self, prior: np.ndarray, bel: np.ndarray, envs=None) -> None:
+        """Per-cell float beliefs of the reference GPU rollout, initialised in
+        place in ``bel`` (N, 4, 12, 289) for ``envs`` (default all):
+        belief_init_kernel, belief.cu:172-248."""
+        pr = np.ascontiguousarray(prior, dtype=np.float32).reshape(30 * 12)
+        assert bel.dtype == np.float32 and bel.shape == (self.n, 4, 12, 289) and bel.flags.c_contiguous
+        for e in range(self.n) if envs is None else envs:
+            lib().jqo_cellbel_init(ctypes.byref(self._c), int(e), _ptr(pr, ctypes.c_float), _ptr(bel, ctypes.c_float))
+
+    def cellbel_update(self, event, flag_captured, world_actions, prev_dead, strongholds, bel: np.ndarray) -> None:
+        """belief_update_kernel (belief.cu:255-565) on this batch's post-step
+        state, in place in ``bel``; prev_dead (N, 4) is the seat_dead
+        snapshot taken before the step, strongholds the 4 x 2 flat cells."""
+        assert bel.dtype == np.float32 and bel.shape == (self.n, 4, 12, 289) and bel.flags.c_contiguous
+        ev = np.asarray(event).astype(np.int64).reshape(self.n)
+        fc = np.asarray(flag_captured).astype(np.int64).reshape(self.n)
+        wa = np.asarray(world_actions).astype(np.int64).reshape(self.n)
+        pd = np.ascontiguousarray(prev_dead, dtype=np.uint8).reshape(self.n, 4)
+        sh = np.ascontiguousarray(strongholds, dtype=np.int16).reshape(8)
+        for e in range(self.n):
+            lib().jqo_cellbel_update(ctypes.byref(self._c), e, int(ev[e]), int(fc[e]), ctypes.c_int32(int(wa[e])),
+                                     _ptr(pd[e], ctypes.c_uint8), _ptr(sh, ctypes.c_int16),
+                                     _ptr(bel, ctypes.c_float))
+
     def obs_one(self, env: int, observer: int):
         sp = np.zeros((OBS_CH, 17, 17), np.float32)
         gl = np.zeros(OBS_GL, np.float32)

@@ -35,7 +35,7 @@ def test_library_exports_every_declared_symbol():
     for s in syms:
         assert hasattr(L, s), f"libjq.so does not export {s}"
     assert set(syms) <= set(N.SIGNATURES), "binding lacks a declared entry point"
-    assert L.jq_abi_version() == 5
+    assert L.jq_abi_version() == 6
 
 
 def test_kernel_board_tables_match_reference():
