@@ -151,3 +151,63 @@ def test_legal_action_mask_batch_is_the_80_slot_mask():
     assert m.shape == (n, 120, 80) and m.dtype == bool
     exp, _ = orc.slot_mask(seats)
     assert np.array_equal(m, exp)
+
+
+def test_reference_gpu_belief_calls_follow_the_oracle():
+    """use_reference_gpu_beliefs(True): the reference's belief calls
+    (init_all_beliefs, snapshot_pre_step_flags, update_beliefs_after_step,
+    init_beliefs_for_reset_envs) keep a resident per-cell tensor equal to
+    the oracle's restatement of belief.cu, and the resident observation
+    reads it."""
+    _setup()
+    n = 16
+    pool = tables.build_setup_pool(n, seed=57)
+    orc = O.OracleBatch(n, 2, rules=1)
+    for e in range(n):
+        orc.reset_env(e, pool[e])
+    state = jc.DeviceGameStateBatch(n, rules=1)
+    state.copy_from_host(_pack(orc))
+    state.copy_termination_from_host(np.zeros(n, bool), np.full(n, -1, np.int8), np.zeros(n, bool))
+    prior = tables.prior_table()
+    zx, zy = orc["zero_x"][0].astype(int), orc["zero_y"][0].astype(int)
+    sh = np.array([zy[s * 30 + k] * 17 + zx[s * 30 + k] for s in range(4) for k in (26, 28)], np.int16)
+    jc.upload_belief_prior_table(prior.ravel())
+    jc.upload_seat_strongholds(sh)
+    jc.use_reference_gpu_beliefs(True)
+    try:
+        jc.init_all_beliefs(state)
+        bel = np.zeros((n, 4, 12, 289), np.float32)
+        orc.cellbel_init(prior, bel)
+        assert np.array_equal(jc._beliefs.cpu().numpy(), bel)
+        rng = np.random.default_rng(5)
+        for t in range(60):
+            off, val = orc.legal()
+            acts = np.array([val[off[e] + rng.integers(off[e + 1] - off[e])] if off[e + 1] > off[e] else -1
+                             for e in range(n)], np.int32)
+            prev_dead = orc["seat_dead"].copy()
+            jc.snapshot_pre_step_flags(state)
+            state.step_batch(acts)
+            d_acts = torch.from_numpy(acts).cuda()
+            jc.update_beliefs_after_step(state, state._out["event"].data_ptr(),
+                                         state._out["flag_captured"].data_ptr(), d_acts.data_ptr())
+            r = orc.step(acts)
+            orc.cellbel_update(r["event"], r["flag_captured"], acts, prev_dead, sh, bel)
+            assert np.array_equal(jc._beliefs.cpu().numpy(), bel), t
+        # re-seed the envs a snapshot sees terminated, as after a reset
+        term = np.zeros(n, bool)
+        term[::3] = True
+        state.copy_termination_from_host(term, np.full(n, -1, np.int8), np.zeros(n, bool))
+        jc.snapshot_pre_step_flags(state)
+        jc.init_beliefs_for_reset_envs(state)
+        orc.cellbel_init(prior, bel, envs=np.nonzero(term)[0])
+        assert np.array_equal(jc._beliefs.cpu().numpy(), bel)
+        # the resident observation reads the tensor
+        jc.upload_observer_seats(n, np.tile(np.arange(4, dtype=np.int8), (n, 1)))
+        obs = jc.DeviceObservationBatch(n)
+        jc.build_observation_batch_resident(state, obs, 2)
+        sp, _ = obs.copy_to_host()
+        o_sp, _ = orc.obs_beliefs(bel, observers=np.zeros(n, np.int8))
+        assert np.array_equal(np.asarray(sp).reshape(n, 4, 317, 17, 17)[:, 0, 12:51], o_sp[:, 12:51])
+    finally:
+        jc.use_reference_gpu_beliefs(False)
+        jc.gpu_scratch_reset()
