@@ -16,7 +16,7 @@
 #include <stddef.h>
 #include <stdint.h>
 
-#define JQ_ABI_VERSION 6
+#define JQ_ABI_VERSION 7
 
 #define JQ_NUM_PIECES 120
 #define JQ_NUM_CELLS 289
@@ -93,6 +93,9 @@ typedef struct jq_batch {
     uint8_t *rem_tracked;              /* (4,4)  bool */
     int32_t rules;                     /* JQ_RULES_BATCHED or JQ_RULES_GAMESTATE */
     int32_t max_moves;                 /* episode cap in plies, 0: the rules' 4000 (see below) */
+    const int8_t *pool;                /* (pool_size,120) setup lineups the resets of this batch
+                                          draw from; NULL: the device-wide pool (jq_set_setup_pool) */
+    int32_t pool_size;
 } jq_batch;
 
 /* jq_batch.max_moves: a game that reaches this many plies without a natural
@@ -150,9 +153,12 @@ int jq_upload_zobrist(const int64_t *piece /*120*14*289*/, const int64_t *turn /
 int jq_upload_obs_tables(const float *prior /*30*12*/, const float *uniform12,
                          const float *recency /*4*4097*/);
 
-/* Register the device-resident setup pool ((P,120) int8, piece type per
- * pid, 0 on camp slots).  The pointer is kept until the next call.
- * Replaces upload_setup_pool (bindings.cpp:1209-1222). */
+/* Register the device-wide setup pool ((P,120) int8, piece type per pid,
+ * 0 on camp slots): the pool of every batch whose own jq_batch.pool is
+ * NULL.  The pointer is kept until the next call, so the caller keeps the
+ * memory alive that long.  Replaces upload_setup_pool (bindings.cpp:1209-
+ * 1222), whose pool is process-global as this one is; a caller with several
+ * batches gives each its own jq_batch.pool instead. */
 int jq_set_setup_pool(const int8_t *d_pool, int32_t pool_size);
 
 /* Pool index used by every reset: splitmix64(seed, ply, env) mod P. */

@@ -42,7 +42,8 @@ BATCH_FIELDS = [
 
 class JqBatch(ctypes.Structure):
     _fields_ = [("n", ctypes.c_int32)] + [(n, ctypes.c_void_p) for n, _ in BATCH_FIELDS] + \
-        [("rules", ctypes.c_int32), ("max_moves", ctypes.c_int32)]
+        [("rules", ctypes.c_int32), ("max_moves", ctypes.c_int32), ("pool", ctypes.c_void_p),
+         ("pool_size", ctypes.c_int32)]
 
 
 RULES_BATCHED, RULES_GAMESTATE = 0, 1

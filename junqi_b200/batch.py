@@ -63,6 +63,7 @@ class DeviceBatch:
         self._struct = N.JqBatch()
         self._struct.n = self.n
         self._struct.rules = int(rules)
+        self._pool = None
         self.max_moves = max_moves
         for name, _, _, _ in FIELDS:
             setattr(self._struct, name, self.t[name].data_ptr())
@@ -88,6 +89,23 @@ class DeviceBatch:
             raise ValueError(f"max_moves must be >= 0, got {m}")
         self._struct.max_moves = int(m)
 
+    def set_pool(self, pool: torch.Tensor | None) -> None:
+        """Setup pool ((P, 120) int8 device tensor) the resets of this batch
+        draw from; None: the device-wide pool of jq_set_setup_pool.  The
+        batch keeps a reference, so the memory outlives every launch."""
+        if pool is None:
+            self._pool = None
+            self._struct.pool = None
+            self._struct.pool_size = 0
+            return
+        if pool.dtype != torch.int8 or pool.dim() != 2 or pool.shape[1] != 120 or not pool.is_contiguous():
+            raise ValueError("pool must be a contiguous (P, 120) int8 tensor")
+        if pool.device.type != "cuda" or (self.device.index is not None and pool.device.index != self.device.index):
+            raise ValueError(f"pool is on {pool.device}, the batch on {self.device}")
+        self._pool = pool
+        self._struct.pool = pool.data_ptr()
+        self._struct.pool_size = int(pool.shape[0])
+
     @property
     def struct(self) -> N.JqBatch:
         return self._struct
@@ -100,6 +118,8 @@ class DeviceBatch:
         s.n = int(count)
         s.rules = self._struct.rules
         s.max_moves = self._struct.max_moves
+        s.pool = self._struct.pool
+        s.pool_size = self._struct.pool_size
         for name, _, _, _ in FIELDS:
             t = self.t[name]
             setattr(s, name, t.data_ptr() + start * t.stride(0) * t.element_size())

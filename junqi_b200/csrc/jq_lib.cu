@@ -434,11 +434,13 @@ static int rules_common(RuleArgs &a, const jq_batch *b, int mode, bool need_zob,
     rc = current_dev(st);
     if (rc) return rc;
     if (need_zob && !st->zob) return fail(JQ_ERR_NOT_READY, "Zobrist tables not uploaded");
+    if (b->pool && b->pool_size <= 0) return fail(JQ_ERR_ARG, "jq_batch.pool given with pool_size <= 0");
     std::memset(&a, 0, sizeof a);
     a.b = *b;
     a.mode = mode;
-    a.pool = st->pool;
-    a.pool_size = st->pool_size;
+    // the batch's own pool; the device-wide one only when it has none
+    a.pool = b->pool ? b->pool : st->pool;
+    a.pool_size = b->pool ? b->pool_size : st->pool_size;
     (void)stream;
     return JQ_OK;
 }

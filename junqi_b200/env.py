@@ -96,7 +96,8 @@ class JunqiEnvB200:
         tables.validate_pool(pool)
         self.pool_host = pool
         self.pool = torch.from_numpy(pool).to(self.device)
-        N.check(N.lib().jq_set_setup_pool(self.pool.data_ptr(), int(pool.shape[0])), "jq_set_setup_pool")
+        # the batch's own pool: other envs in the process keep theirs
+        self.batch.set_pool(self.pool)
 
     def _ptr(self, t):
         return None if t is None else t.data_ptr()

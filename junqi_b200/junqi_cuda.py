@@ -125,8 +125,10 @@ def upload_belief_prior_table(prior) -> None:
     if p.size != 360:
         raise RuntimeError("upload_belief_prior_table: expected 360 floats")
     _cell_prior = torch.from_numpy(p.copy()).to(f"cuda:{_device}")
-    N.check(N.lib().jq_upload_obs_tables(p.ctypes.data, tables.uniform12().ctypes.data,
-                                         tables.recency_lut().ctypes.data), "jq_upload_obs_tables")
+    # the host tables stay referenced until the upload returns: a pointer
+    # taken from a temporary array would point at freed (and reused) memory
+    uni, rec = tables.uniform12(), tables.recency_lut()
+    N.check(N.lib().jq_upload_obs_tables(p.ctypes.data, uni.ctypes.data, rec.ctypes.data), "jq_upload_obs_tables")
 
 
 def upload_seat_strongholds(strongholds) -> None:
@@ -152,8 +154,13 @@ _cell_prev_term: torch.Tensor | None = None
 
 def use_reference_gpu_beliefs(enabled: bool = True) -> None:
     """Select the reference GPU rollout's per-cell belief rules for the
-    init / snapshot / update belief calls (default: off)."""
-    global _cell_mode
+    init / snapshot / update belief calls (default: off).  Switching the
+    mode off drops the resident per-cell tensor, so later observations use
+    the library's own beliefs again rather than a tensor no step updates."""
+    global _cell_mode, _beliefs, _cell_prev_dead, _cell_prev_term
+    if _cell_mode and not enabled:
+        _beliefs = None
+        _cell_prev_dead = _cell_prev_term = None
     _cell_mode = bool(enabled)
 
 
@@ -182,11 +189,13 @@ def upload_observer_seats(num_envs: int, observer_seats) -> None:
 
 
 def gpu_scratch_reset() -> None:
-    """Forget uploaded beliefs, observer seats and belief snapshots."""
-    global _beliefs, _observer_seats, _cell_prev_dead, _cell_prev_term
+    """Forget uploaded beliefs, observer seats and belief snapshots, and
+    leave the reference per-cell belief mode."""
+    global _beliefs, _observer_seats, _cell_prev_dead, _cell_prev_term, _cell_mode
     _beliefs = None
     _observer_seats = None
     _cell_prev_dead = _cell_prev_term = None
+    _cell_mode = False
 
 
 def device_synchronize() -> None:

@@ -67,11 +67,36 @@ def _as_u8(a):
     return a.astype(np.uint8) if a.dtype == bool else a
 
 
+# every state field an observation reads, including the ones no fixture
+# digest covers (belief codes, inventories, move history)
+SHADOW_KEYS = STATE_KEYS + ["hist_src", "hist_dst", "hist_count", "bel_code", "remaining", "rem_tracked"]
+
+
+def _obs_diff(sp, gl, osp, ogl, limit=12) -> str:
+    sp = np.asarray(sp, np.float32).reshape(317, 17, 17)
+    osp = np.asarray(osp, np.float32).reshape(317, 17, 17)
+    d = np.argwhere(sp.view(np.uint32) != osp.view(np.uint32))
+    parts = [f"ch{c} y{y} x{x}: {sp[c, y, x]!r} vs {osp[c, y, x]!r}" for c, y, x in d[:limit]]
+    g = np.nonzero(np.asarray(gl, np.float32).view(np.uint32) != np.asarray(ogl, np.float32).view(np.uint32))[0]
+    if g.size:
+        parts.append(f"global {g[:limit].tolist()}")
+    return f"{len(d)} planes floats differ; " + "; ".join(parts)
+
+
 def replay(fx: dict, drv, plies: int | None = None, check_obs: bool = True,
-           check_every_cm: bool = True) -> int:
-    """Replay ``fx`` through ``drv``; returns the number of plies checked."""
+           check_every_cm: bool = True, shadow=None) -> int:
+    """Replay ``fx`` through ``drv``; returns the number of plies checked.
+
+    ``shadow``: a second driver (the oracle) stepped in lockstep.  After every
+    ply each field of SHADOW_KEYS must equal the shadow's, so a divergence in
+    a field no fixture digest covers is caught at the ply it happens; an
+    observation that misses its digest is reported as its differing
+    (channel, cell) list against the shadow's."""
     T = fx["actions"].shape[0] if plies is None else min(plies, fx["actions"].shape[0])
-    drv.load(init_state(fx), int(fx["show_mode"]), int(fx["rules"]) if "rules" in fx else 0)
+    show, rules = int(fx["show_mode"]), int(fx["rules"]) if "rules" in fx else 0
+    drv.load(init_state(fx), show, rules)
+    if shadow is not None:
+        shadow.load(init_state(fx), show, rules)
     obs_at: dict[int, list] = {}
     for (t, e, s), h in zip(fx["obs_keys"].tolist(), fx["obs_sha"].tolist()):
         obs_at.setdefault(int(t), []).append((int(e), int(s), h))
@@ -79,8 +104,18 @@ def replay(fx: dict, drv, plies: int | None = None, check_obs: bool = True,
     def check_obs_at(t):
         for e, s, h in obs_at.get(t, []):
             sp, gl = drv.obs(e, s)
-            assert sha(np.asarray(sp, np.float32), np.asarray(gl, np.float32)) == h, \
-                f"observation digest differs at ply {t} env {e} observer {s}"
+            if sha(np.asarray(sp, np.float32), np.asarray(gl, np.float32)) != h:
+                detail = "" if shadow is None else ": " + _obs_diff(sp, gl, *shadow.obs(e, s))
+                raise AssertionError(f"observation digest differs at ply {t} env {e} observer {s}{detail}")
+
+    def check_shadow(t, got):
+        exp = shadow.state()
+        for k in SHADOW_KEYS:
+            a, b = np.asarray(got[k]), np.asarray(exp[k])
+            a = a.reshape(b.shape).astype(b.dtype)
+            if not np.array_equal(a, b):
+                envs = np.nonzero((a != b).reshape(b.shape[0], -1).any(1))[0]
+                raise AssertionError(f"after ply {t}: state field {k} differs from the oracle in envs {envs[:8]}")
 
     for t in range(T):
         if check_obs:
@@ -90,6 +125,8 @@ def replay(fx: dict, drv, plies: int | None = None, check_obs: bool = True,
             f"legal CSR differs at ply {t}"
         assert sha(np.asarray(drv.masks(), bool)) == fx["mask_sha"][t], f"canonical mask differs at ply {t}"
         r = drv.step(fx["actions"][t])
+        if shadow is not None:
+            shadow.step(fx["actions"][t])
         for k, rk in (("valid", "res_valid"), ("event", "res_event"), ("terminated", "res_terminated"),
                       ("winner", "res_winner"), ("draw", "res_draw"), ("flag_captured", "res_flag")):
             got = np.asarray(r[k]).astype(np.int8)
@@ -100,6 +137,8 @@ def replay(fx: dict, drv, plies: int | None = None, check_obs: bool = True,
         assert bad.size == 0, f"zobrist differs at ply {t}, envs {bad[:8]}"
         if check_every_cm or t == T - 1:
             assert sha(*[_as_u8(st[k]) for k in CM_ORDER]) == fx["cm_sha"][t], f"combat memory differs at ply {t}"
+        if shadow is not None:
+            check_shadow(t, st)
     if check_obs and T == fx["actions"].shape[0]:
         check_obs_at(T)
     if T == fx["actions"].shape[0]:

@@ -189,3 +189,32 @@ def test_belief_sweep_repairs_codes_written_by_the_host():
     alive = np.asarray(env.state()["alive"]).reshape(n, 120).astype(bool)[stepped]
     assert ((fixed != 0) == alive[:, None, :]).all()
     _compare_obs(env, orc, 3, seats=1)
+
+
+def test_each_env_resets_from_its_own_pool():
+    """The setup pool belongs to the batch (jq_batch.pool): two envs alive in
+    one process with different pools each reset from their own, whichever
+    was built last, and an env's pool outlives another env's."""
+    pa = tables.build_setup_pool(16, seed=101)
+    pb = tables.build_setup_pool(9, seed=202)
+    a = JunqiEnvB200(32, pool=pa, with_obs=False)
+    b = JunqiEnvB200(32, pool=pb, with_obs=False)
+    L = N.lib()
+    for env, pool, seed in ((a, pa, 7), (b, pb, 8), (a, pa, 9)):
+        env.reset(seed=seed)
+        got = env.batch["piece_type"].cpu().numpy()
+        for e in range(env.n):
+            lineup = pool[L.jq_pool_index(seed, 0, e, pool.shape[0])]
+            exp = np.where(lineup != 0, lineup, -1)
+            assert np.array_equal(got[e], exp), (seed, e)
+    del b
+    import gc
+    gc.collect()
+    torch.cuda.empty_cache()
+    junk = torch.full((1 << 20,), 3, dtype=torch.int8, device="cuda")  # reuse freed memory
+    a.reset(seed=10)
+    got = a.batch["piece_type"].cpu().numpy()
+    for e in range(a.n):
+        lineup = pa[L.jq_pool_index(10, 0, e, pa.shape[0])]
+        assert np.array_equal(got[e], np.where(lineup != 0, lineup, -1))
+    del junk

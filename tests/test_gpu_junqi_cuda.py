@@ -211,3 +211,43 @@ def test_reference_gpu_belief_calls_follow_the_oracle():
     finally:
         jc.use_reference_gpu_beliefs(False)
         jc.gpu_scratch_reset()
+
+
+def test_leaving_reference_belief_mode_restores_default_observations():
+    """use_reference_gpu_beliefs(False) drops the resident per-cell tensor:
+    the next resident observation is the default-mode one again, and
+    gpu_scratch_reset also leaves the mode."""
+    _setup()
+    n = 12
+    pool = tables.build_setup_pool(n, seed=61)
+    orc = O.OracleBatch(n, 2, rules=1)
+    for e in range(n):
+        orc.reset_env(e, pool[e])
+    state = jc.DeviceGameStateBatch(n, rules=1)
+    state.copy_from_host(_pack(orc))
+    state.copy_termination_from_host(np.zeros(n, bool), np.full(n, -1, np.int8), np.zeros(n, bool))
+    jc.init_all_beliefs(state)
+    jc.upload_observer_seats(n, np.tile(np.arange(4, dtype=np.int8), (n, 1)))
+    obs = jc.DeviceObservationBatch(n)
+    jc.build_observation_batch_resident(state, obs, 2)
+    default_sp, default_gl = (np.array(a) for a in obs.copy_to_host())
+    prior = tables.prior_table()
+    zx, zy = orc["zero_x"][0].astype(int), orc["zero_y"][0].astype(int)
+    sh = np.array([zy[s * 30 + k] * 17 + zx[s * 30 + k] for s in range(4) for k in (26, 28)], np.int16)
+    jc.upload_belief_prior_table(prior.ravel())
+    jc.upload_seat_strongholds(sh)
+    jc.use_reference_gpu_beliefs(True)
+    try:
+        jc.init_all_beliefs(state)
+        assert jc._beliefs is not None
+        jc.use_reference_gpu_beliefs(False)
+        assert jc._beliefs is None
+        jc.build_observation_batch_resident(state, obs, 2)
+        sp, gl = obs.copy_to_host()
+        assert np.array_equal(sp, default_sp) and np.array_equal(gl, default_gl)
+        jc.use_reference_gpu_beliefs(True)
+        jc.gpu_scratch_reset()
+        assert not jc._cell_mode and jc._beliefs is None
+    finally:
+        jc.use_reference_gpu_beliefs(False)
+        jc.gpu_scratch_reset()

@@ -63,8 +63,11 @@ class CudaDriver:
 
 @pytest.mark.parametrize("name", G.TRAJECTORIES)
 def test_cuda_replays_reference_trajectory(name):
+    """Every recorded digest, and after every ply every field the
+    observation reads against the oracle stepped in lockstep."""
+    from tests.test_oracle_golden import OracleDriver
     fx = G.load(name)
-    assert G.replay(fx, CudaDriver()) == fx["actions"].shape[0]
+    assert G.replay(fx, CudaDriver(), shadow=OracleDriver()) == fx["actions"].shape[0]
 
 
 # ---------------------------------------------------------------------------

@@ -35,7 +35,7 @@ def test_library_exports_every_declared_symbol():
     for s in syms:
         assert hasattr(L, s), f"libjq.so does not export {s}"
     assert set(syms) <= set(N.SIGNATURES), "binding lacks a declared entry point"
-    assert L.jq_abi_version() == 6
+    assert L.jq_abi_version() == 7
 
 
 def test_kernel_board_tables_match_reference():
@@ -105,3 +105,20 @@ def test_history_record_is_compact_and_aligned():
     smaller than the 366 KB observation it rebuilds."""
     size = N.lib().jq_history_record_bytes()
     assert size % 16 == 0 and 8_000 <= size <= 16_384
+
+
+def test_no_host_pointer_is_taken_from_a_temporary_array():
+    """``f(make_table().ctypes.data)`` hands the library a pointer into an
+    array CPython frees before the call runs (only the integer survives);
+    the C side then copies freed, possibly reused, heap memory -- a device
+    table uploaded that way is corrupt for the rest of the process.  Host
+    code must keep every array it passes by pointer in a named variable."""
+    import re
+    from pathlib import Path
+    root = Path(__file__).resolve().parent.parent
+    bad = []
+    for p in [*sorted((root / "junqi_b200").glob("*.py")), root / "bench.py", root / "__graft_entry__.py"]:
+        for i, line in enumerate(p.read_text().splitlines(), 1):
+            if re.search(r"\)\s*\.ctypes\.data\b", line):
+                bad.append(f"{p.name}:{i}: {line.strip()}")
+    assert not bad, "pointers taken from temporaries:\n" + "\n".join(bad)
