@@ -143,8 +143,9 @@ def profiled_traffic(cfg: str) -> float | None:
 # ---------------------------------------------------------------------------
 
 def cpu_rollout(envs: int, plies: int, seats: int, seed: int, threads: int, budget_s: float, rules: int = 1,
-                late: bool = False):
-    """Step + legal + observation on the CPU oracle; returns (plies/s, plies, seconds, sample text)."""
+                late: bool = False, burn_in: int = 0):
+    """Step + legal + observation on the CPU oracle; returns (plies/s, plies, seconds, sample text).
+    ``burn_in`` untimed plies (step + legal, no observation) come first, as in the GPU arm."""
     os.environ["JQ_ORACLE_THREADS"] = str(threads)
     from junqi_b200 import tables
     from oracle import oracle as O
@@ -158,6 +159,16 @@ def cpu_rollout(envs: int, plies: int, seats: int, seed: int, threads: int, budg
         from junqi_b200 import workloads
         O.load_state(b, workloads.thin_positions({k: v.copy() for k, v in b.a.items()}, seed), init_beliefs=True)
         b.a["zobrist"][:] = O.zobrist_recompute(b.a, 2)
+    def pick_actions():
+        off, val = b.legal()
+        cnt = np.diff(off)
+        pick = (rng.random(envs) * np.maximum(cnt, 1)).astype(np.int64)
+        return np.where(cnt > 0, val[np.minimum(off[:-1] + pick, max(len(val) - 1, 0))] if len(val) else -1, -1)
+
+    for _ in range(burn_in):
+        r = b.step(pick_actions().astype(np.int32))
+        for e in np.nonzero(r["terminated"])[0]:
+            b.reset_env(int(e), pool[int(rng.integers(len(pool)))])
     done = 0
     t0 = time.perf_counter()
     t = 0
@@ -167,18 +178,15 @@ def cpu_rollout(envs: int, plies: int, seats: int, seed: int, threads: int, budg
         else:
             for s in range(4):
                 b.obs(np.full(envs, s, np.int8))
-        off, val = b.legal()
-        cnt = np.diff(off)
-        pick = (rng.random(envs) * np.maximum(cnt, 1)).astype(np.int64)
-        acts = np.where(cnt > 0, val[np.minimum(off[:-1] + pick, max(len(val) - 1, 0))] if len(val) else -1, -1)
-        r = b.step(acts.astype(np.int32))
+        r = b.step(pick_actions().astype(np.int32))
         done += int(r["valid"].sum())
         for e in np.nonzero(r["terminated"])[0]:
             b.reset_env(int(e), pool[int(rng.integers(len(pool)))])
         if time.perf_counter() - t0 > budget_s:
             break
     dt = time.perf_counter() - t0
-    sample = f"{envs} envs x {t + 1} plies, step + legal + obs ({seats} seat/env), {threads} threads"
+    sample = (f"{envs} envs x {t + 1} plies after a {burn_in}-ply burn-in, step + legal + obs ({seats} seat/env), "
+              f"{threads} threads")
     return done / dt, done, dt, sample
 
 
@@ -200,13 +208,12 @@ def reference_arm(args, cfg: dict) -> None:
     for _ in range(args.warmup if args.warmup < 3 else 2):
         cpu_rollout(min(envs, 64), 1, cfg["seats"], args.seed, threads, 5.0, RULES[args.rules])
     rate, done, dt, sample = cpu_rollout(envs, args.steps, cfg["seats"], args.seed, threads, 120.0,
-                                         RULES[args.rules], late=cfg.get("start") == "late")
+                                         RULES[args.rules], late=cfg.get("start") == "late", burn_in=args.burn_in)
     line = {"impl": "reference", "metric": "env plies/s (step + legal mask + 317-ch obs)", "value": rate,
             "unit": "plies/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8/int16/f32",
-            "data": "synthetic (seeded setup pool, uniform-random legal policy)",
-            "config": {"workload": cfg["workload"], "envs_sampled": envs, "seats_per_env": cfg["seats"],
-                       "rules": RULES_TEXT[args.rules]},
+            "data": "synthetic (seeded setup pool of random legal lineups, seeded policy)",
+            "config": arm_config(cfg, args, args.gpus),
             "cpu_baseline": {"value": rate, "unit": "plies/s", "cores": threads, "kind": "port",
                              "sample": sample + f", {dt:.1f} s"},
             "e2e": {"value": rate, "unit": "plies/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -287,11 +294,24 @@ def reference_cuda_arm(args, cfg: dict) -> None:
 # GPU arm
 # ---------------------------------------------------------------------------
 
+def arm_config(cfg: dict, args, world: int) -> dict:
+    """The workload description both arms print (the reference arm times a
+    bounded sample of this same workload; its sample is in cpu_baseline)."""
+    return {"workload": cfg["workload"], "envs_per_gpu": cfg["envs"], "seats_per_env": cfg["seats"],
+            "policy": cfg["policy"], "show_mode": "HALF_DARK", "rules": RULES_TEXT[args.rules],
+            "burn_in_plies": args.burn_in,
+            "l2": "per-step output (obs) > 1.5 GB >> 126 MB L2; no flush needed",
+            "parallelism": f"env-sharded x{world} (weak)"}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=None, help="timed plies (default: the config's plies)")
     ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--burn-in", type=int, default=200,
+                    help="untimed plies played before the warm-up, so the timed plies sample a rollout's steady "
+                         "mix of openings, combat, finished games and resets rather than only fresh games")
     ap.add_argument("--impl", default="b200", choices=["b200", "reference", "reference-cuda"])
     ap.add_argument("--config", default="cfg2", choices=sorted(CONFIGS))
     ap.add_argument("--envs", type=int, default=None, help="envs per GPU (default: the config's)")
@@ -299,6 +319,9 @@ def main() -> None:
     ap.add_argument("--seed", type=int, default=2026)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-pin", action="store_true", help="do not restrict each rank to its share of host cores")
+    ap.add_argument("--collector", action="store_true",
+                    help="time RolloutCollector (eager vs one CUDA graph per rollout) instead; one line per case")
     ap.add_argument("--rules", default="gamestate", choices=sorted(RULES),
                     help="turn-advance rules: GameState.step (default) or BatchedGameState.step_batch")
     args = ap.parse_args()
@@ -313,6 +336,9 @@ def main() -> None:
     if args.impl == "reference":
         reference_arm(args, cfg)
         return
+    if args.collector:
+        collector_bench(args)
+        return
 
     import torch
     import torch.distributed as dist
@@ -320,6 +346,9 @@ def main() -> None:
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    local_world = int(os.environ.get("LOCAL_WORLD_SIZE", str(world)))
+    from junqi_b200 import sharding
+    cores = sharding.pin_rank_cores(local, local_world) if world > 1 and not args.no_pin else None
     torch.cuda.set_device(local)
     if world > 1:
         import datetime
@@ -327,7 +356,6 @@ def main() -> None:
                                 device_id=torch.device("cuda", local))
 
     from junqi_b200 import _native
-    from junqi_b200 import sharding
     from junqi_b200 import tables
     from junqi_b200.env import JunqiEnvB200
     _native.build()
@@ -358,25 +386,36 @@ def main() -> None:
         if ev is not None:
             ev[3].record(stream)
 
-    for t in range(1, args.warmup + 1):  # same ops as the timed loop, so every kernel is loaded
+    # clocks are sampled from the burn-in on, so the GPU never idles between
+    # the warm-up and the timed plies (an idle gap lets it leave its loaded
+    # state and slows the first timed plies)
+    clock_rows, stop = [], threading.Event()
+    th = threading.Thread(target=sample_clocks, args=(local, stop, clock_rows), daemon=True)
+    th.start()
+    t = 0
+    for t in range(1, args.burn_in + 1):
+        one_ply(t)
+    for t in range(args.burn_in + 1, args.burn_in + args.warmup + 1):  # the timed loop's ops, events included
         one_ply(t, [torch.cuda.Event(enable_timing=True) for _ in range(4)] if t % EVENT_EVERY == 0 else None)
+    t0_ply = t + 1
     env.stats.zero_()  # jq_ply counts plies applied and episode statistics on the device
     # Per-kernel CUDA events on every EVENT_EVERY-th timed ply: an event between
     # two kernels keeps the next launch from overlapping the previous one's tail.
     evs = {k: [torch.cuda.Event(enable_timing=True) for _ in range(4)] for k in range(0, args.steps, EVENT_EVERY)}
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    clock_rows, stop = [], threading.Event()
-    th = threading.Thread(target=sample_clocks, args=(local, stop, clock_rows), daemon=True)
-    th.start()
-    time.sleep(0.5)
+    start, end, ar0 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
+        # Leave the barrier on the device: every GPU starts its timed plies
+        # when this all-reduce completes on all of them, not when its host
+        # got there, so host launch skew stays out of the max over ranks.
+        align = torch.zeros(1, dtype=torch.int64, device=env.device)
+        dist.all_reduce(align)
     t_wall = time.perf_counter()
     start.record(stream)
     for k in range(args.steps):
-        t = args.warmup + 1 + k
-        one_ply(t, evs.get(k))
+        one_ply(t0_ply + k, evs.get(k))
+    ar0.record(stream)
     if world > 1:
         sharding.reduce_episode_stats(env.stats)  # one collective per rollout: episode statistics
     end.record(stream)
@@ -384,8 +423,6 @@ def main() -> None:
     t_wall = time.perf_counter() - t_wall
     if world > 1:
         dist.barrier()
-    stop.set()
-    th.join(timeout=10)
     ms_total = start.elapsed_time(end)
     obs_ms = [e[0].elapsed_time(e[1]) for e in evs.values()]
     ply_ms = [e[2].elapsed_time(e[3]) for e in evs.values()]
@@ -400,6 +437,15 @@ def main() -> None:
     e2e = None
     if not args.no_e2e:
         e2e = run_e2e(env, args, seed, stream)
+    stop.set()
+    th.join(timeout=10)
+    mine = {"rank": rank, "device_ms": round(ms_total, 4), "plies_ms": round(start.elapsed_time(ar0), 4),
+            "allreduce_ms": round(ar0.elapsed_time(end), 4),
+            "obs_kernel_ms": round(statistics.mean(obs_ms), 4), "ply_kernel_ms": round(statistics.mean(ply_ms), 4),
+            "host_cores": None if cores is None else len(cores)}
+    if e2e is not None:
+        mine.update({k: e2e.pop(k) for k in ("e2e_ms_per_step", "host_ms_per_step", "wait_ms_per_step")})
+    per_rank = sharding.gather_over_ranks(mine)
     if rank == 0:
         peak, peak_kind = peak_hbm()
         units = n * seats
@@ -407,16 +453,15 @@ def main() -> None:
         obs_avg = statistics.mean(obs_ms)
         achieved = obs_bytes / (obs_avg / 1e3) / 1e9
         traffic_unit = profiled_traffic(args.config)
+        config = arm_config(cfg, args, world)
+        config["timed_plies"] = f"{t0_ply}..{t0_ply + args.steps - 1} of each env batch's rollout"
         line = {
             "metric": "env plies/s (step + legal mask + 317-ch obs)", "value": value, "unit": "plies/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8/int16/f32",
             "data": "synthetic (seeded setup pool of random legal lineups, seeded policy)",
-            "config": {"workload": cfg["workload"], "envs_per_gpu": n, "seats_per_env": seats,
-                       "policy": cfg["policy"], "show_mode": "HALF_DARK", "plies_applied": plies_all,
-                       "plies_offered": n * world * args.steps, "rules": RULES_TEXT[args.rules],
-                       "l2": "per-step output (obs) > 1.5 GB >> 126 MB L2; no flush needed",
-                       "parallelism": f"env-sharded x{world} (weak)"},
+            "config": config,
+            "plies_applied": plies_all, "plies_offered": n * world * args.steps,
             "roofline": {"bound": "hbm", "kernel": "obs_kernel", "achieved": achieved, "peak": peak,
                          "unit": "GB/s", "frac": achieved / peak, "peak_kind": peak_kind,
                          "traffic": None if traffic_unit is None else traffic_unit * units,
@@ -429,6 +474,7 @@ def main() -> None:
                              f"({len(obs_ms)} plies)",
             "episode_stats": {"wins_team0": stats[0], "wins_team1": stats[1], "draws": stats[2],
                               "episodes": stats[3], "sum_len": stats[4]},
+            "per_rank": per_rank,
             "wall_s": t_wall,
         }
         if e2e is not None:
@@ -436,7 +482,8 @@ def main() -> None:
         if not args.no_cpu_baseline:
             threads = host_cores()
             rate, done, dt, sample = cpu_rollout(min(n, 64 * threads), 400, seats, args.seed, threads, 15.0,
-                                                 RULES[args.rules], late=cfg.get("start") == "late")
+                                                 RULES[args.rules], late=cfg.get("start") == "late",
+                                                 burn_in=min(args.burn_in, 100))
             line["cpu_baseline"] = {"value": rate, "unit": "plies/s", "cores": threads, "kind": "port",
                                     "sample": sample + f", {dt:.1f} s"}
         print(json.dumps(line), flush=True)
@@ -445,73 +492,146 @@ def main() -> None:
 
 
 def run_e2e(env, args, seed, stream) -> dict:
-    """Same metric through the public API with host buffers every step."""
+    """Same metric through the public API with host buffers every step.
+
+    Per ply the host picks actions from the previous ply's CSR, uploads them
+    from pinned memory, launches ply + CSR + observation, and reads back the
+    MoveResult and the CSR -- one copy of a prefix of the env's io buffer,
+    which holds the results, the offsets and the values in that order -- on
+    a side stream as soon as the CSR is built, while the observation kernel
+    keeps running on the main stream.  The values are read up to a bound
+    that grows with the largest CSR seen, so the host blocks once per ply; a
+    CSR beyond the bound costs a second, rare, read."""
     import torch
     n = env.n
+    np_type = {torch.uint8: np.uint8, torch.int8: np.int8, torch.int32: np.int32, torch.int64: np.int64,
+               torch.float32: np.float32}
     acts_h = torch.empty(n, dtype=torch.int32, pin_memory=True)
-    res_h = {k: torch.empty(n, dtype=v.dtype, pin_memory=True) for k, v in env.out.items()
-             if k in ("valid", "event", "terminated", "winner", "draw", "reward")}
-    off_h = torch.empty(n + 1, dtype=torch.int32, pin_memory=True)
-    val_h = torch.empty(n * env.cap, dtype=torch.int32, pin_memory=True)
+    io_h = torch.empty(env.io.numel(), dtype=torch.uint8, pin_memory=True)
+    io_np = io_h.numpy()
+
+    def view(t):  # the host image of a view of env.io
+        o = t.data_ptr() - env.io.data_ptr()
+        return io_np[o:o + t.numel() * t.element_size()].view(np_type[t.dtype])
+
+    off_np, val_np, valid_np = view(env.offsets), view(env.values), view(env.out["valid"])
     acts_d = torch.empty(n, dtype=torch.int32, device=env.device)
     rng = np.random.default_rng(seed)
     env.legal()
-    off, val = env.csr()
-    off_h.copy_(off)
+    env.csr()
     torch.cuda.synchronize()
-    tot = int(off_h[-1])
-    val_h[:tot].copy_(val[:tot])
-    applied, h2d, d2h = 0, 0, 0
+    io_h[: env.io_prefix_bytes(0)].copy_(env.io[: env.io_prefix_bytes(0)])
+    tot = int(off_np[-1])
+    io_h[: env.io_prefix_bytes(tot)].copy_(env.io[: env.io_prefix_bytes(tot)])
+    bound = min(n * env.cap, max(4 * n, tot + tot // 4))
+    applied, h2d, d2h, extra_reads = 0, 0, 0, 0
     steps = args.e2e_steps
+    host_s = wait_s = 0.0
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    # The host needs only the step results and the legal CSR to choose the next
-    # actions; they are copied on a side stream as soon as the ply is done,
-    # while the observation kernel (consumed on the device by the policy) keeps
-    # running on the main stream.
     copy_stream = torch.cuda.Stream(device=env.device)
-    csr_done, acts_up = torch.cuda.Event(), torch.cuda.Event()
+    csr_done, acts_up, copies_done = torch.cuda.Event(), torch.cuda.Event(), torch.cuda.Event()
     torch.cuda.synchronize()
     import torch.distributed as dist
     if dist.is_initialized():
         dist.barrier()
     start.record(stream)
     for t in range(steps):
-        o = off_h.numpy()
-        cnt = np.diff(o)
+        h0 = time.perf_counter()
+        cnt = np.diff(off_np)
         pick = (rng.random(n) * np.maximum(cnt, 1)).astype(np.int64)
-        v = val_h.numpy()
-        acts_h.numpy()[:] = np.where(cnt > 0, v[np.minimum(o[:-1] + pick, max(int(o[-1]) - 1, 0))], -1)
+        acts_h.numpy()[:] = np.where(cnt > 0, val_np[np.minimum(off_np[:-1] + pick, max(int(off_np[-1]) - 1, 0))],
+                                     -1)
         with torch.cuda.stream(copy_stream):  # upload under the observation kernel still running
             acts_d.copy_(acts_h, non_blocking=True)
             acts_up.record(copy_stream)
         h2d += n * 4
         stream.wait_event(acts_up)
         env.ply(acts_d, seed=seed, ply=100_000 + t)
-        off, val = env.csr()
+        env.csr()
         csr_done.record(stream)
         env.observe()
+        nb = env.io_prefix_bytes(bound)
         with torch.cuda.stream(copy_stream):
             copy_stream.wait_event(csr_done)
-            for k, h in res_h.items():
-                h.copy_(env.out[k], non_blocking=True)
-                d2h += h.numel() * h.element_size()
-            off_h.copy_(off, non_blocking=True)
-        copy_stream.synchronize()
-        tot = int(off_h[-1])
-        with torch.cuda.stream(copy_stream):
-            val_h[:tot].copy_(val[:tot], non_blocking=True)
-        copy_stream.synchronize()
-        d2h += (n + 1) * 4 + tot * 4
-        applied += int(res_h["valid"].numpy().sum())
+            io_h[:nb].copy_(env.io[:nb], non_blocking=True)
+            copies_done.record(copy_stream)
+        d2h += nb
+        h1 = time.perf_counter()
+        copies_done.synchronize()  # the one blocking wait of the ply
+        h2 = time.perf_counter()
+        tot = int(off_np[-1])
+        if tot > bound:  # a CSR larger than any seen so far
+            nt = env.io_prefix_bytes(tot)
+            with torch.cuda.stream(copy_stream):
+                io_h[nb:nt].copy_(env.io[nb:nt], non_blocking=True)
+            copy_stream.synchronize()
+            d2h += nt - nb
+            extra_reads += 1
+            bound = min(n * env.cap, tot + tot // 4)
+        applied += int(valid_np.sum(dtype=np.int64))
+        host_s += (h1 - h0) + (time.perf_counter() - h2)
+        wait_s += h2 - h1
     end.record(stream)
     torch.cuda.synchronize()
     from junqi_b200 import sharding
-    ms = sharding.max_over_ranks(start.elapsed_time(end), env.device)
+    ms_own = start.elapsed_time(end)
+    ms = sharding.max_over_ranks(ms_own, env.device)
     applied = sharding.sum_over_ranks(applied, env.device)
     return {"value": applied / (ms / 1e3), "unit": "plies/s", "h2d_bytes_per_step": h2d // steps,
-            "d2h_bytes_per_step": d2h // steps, "steps": steps,
-            "api": "JunqiEnvB200.ply/csr/observe with pinned host actions in, MoveResult + CSR out (upload and "
-                   "copies on a side stream overlap the observation kernel)"}
+            "d2h_bytes_per_step": d2h // steps, "steps": steps, "extra_csr_reads": extra_reads,
+            "e2e_ms_per_step": round(ms_own / steps, 4), "host_ms_per_step": round(host_s * 1e3 / steps, 4),
+            "wait_ms_per_step": round(wait_s * 1e3 / steps, 4),
+            "api": "JunqiEnvB200.ply/csr/observe with pinned host actions in; MoveResult + CSR out as one read "
+                   "per ply on a side stream, overlapping the observation kernel"}
+
+
+class _ArgmaxPolicy:
+    """Stand-in for a network: masked argmax over fixed random per-action
+    scores (one pass over the canonical mask), so the collector's own cost
+    shows."""
+
+    def __init__(self, device):
+        import torch
+        g = torch.Generator(device="cpu").manual_seed(0)
+        self.score = torch.rand(16641, generator=g).to(device)
+
+    def __call__(self, sp, gl, mask):
+        import torch
+        v, a = torch.where(mask, self.score, -1.0).max(1)
+        return a, v, gl[:, 0]
+
+
+def collector_bench(args) -> None:
+    """RolloutCollector throughput, eager against one CUDA graph per
+    rollout (GameState rules, HALF_DARK, compact history on): one JSON line
+    per (envs, mode).  --envs sets the batch (default 256 and 4096), --steps
+    the plies per rollout (default 64)."""
+    import torch
+    from junqi_b200 import _native as N
+    from junqi_b200 import tables
+    from junqi_b200.collector import RolloutCollector
+    from junqi_b200.env import HALF_DARK, JunqiEnvB200
+    N.build()
+    pool = tables.build_setup_pool(1024, seed=2)
+    plies = args.steps if args.steps and args.steps != CONFIGS[args.config]["plies"] else 64
+    for n in ([args.envs] if args.envs else [256, 4096]):
+        for graph in (False, True):
+            env = JunqiEnvB200(n, show_mode=HALF_DARK, pool=pool, rules=N.RULES_GAMESTATE)
+            env.reset(seed=1)
+            col = RolloutCollector(env, _ArgmaxPolicy(env.device), plies, seed=3, graph=graph)
+            for _ in range(max(1, args.warmup // 5)):
+                col.collect()
+            torch.cuda.synchronize()
+            t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            t0.record()
+            for _ in range(3):
+                col.collect()
+            t1.record()
+            torch.cuda.synchronize()
+            ms = t0.elapsed_time(t1) / 3
+            print(json.dumps({"collector": True, "envs": n, "plies": plies, "graph": graph,
+                              "ms_per_rollout": round(ms, 3), "plies_per_s": round(plies * n / ms * 1e3)}),
+                  flush=True)
 
 
 if __name__ == "__main__":

@@ -69,16 +69,26 @@ class JunqiEnvB200:
         self.set_pool(pool)
         dev = self.device
         n = self.n
-        self.out = {k: torch.zeros(n, dtype=dt, device=dev) for k, dt in
-                    (("valid", torch.uint8), ("event", torch.int8), ("terminated", torch.uint8),
-                     ("winner", torch.int8), ("draw", torch.uint8), ("flag_captured", torch.uint8),
-                     ("reward", torch.float32), ("world_action", torch.int32), ("zobrist", torch.int64))}
+        # The step results, then the legal CSR (offsets, values), as views of
+        # one device buffer: a host that reads the results and the CSR after
+        # every ply does it with one copy of a prefix of this buffer.
+        fields = (("valid", torch.uint8), ("event", torch.int8), ("terminated", torch.uint8),
+                  ("winner", torch.int8), ("draw", torch.uint8), ("flag_captured", torch.uint8),
+                  ("reward", torch.float32), ("world_action", torch.int32), ("zobrist", torch.int64))
+        layout, pos = [], 0
+        for k, dt in fields + (("offsets", torch.int32),):
+            layout.append((k, dt, pos))
+            pos += -(-(n + (k == "offsets")) * dt.itemsize // 16) * 16
+        self.values_byte_offset = pos
+        self.io = torch.zeros(pos + n * self.cap * 4, dtype=torch.uint8, device=dev)
+        views = {k: self.io[o:o + (n + (k == "offsets")) * dt.itemsize].view(dt) for k, dt, o in layout}
+        self.offsets = views.pop("offsets")
+        self.values = self.io[pos:].view(torch.int32)
+        self.out = views
         self._out = N.JqStepOut(**{k: v.data_ptr() for k, v in self.out.items()})
         self.counts = torch.zeros(n, dtype=torch.int32, device=dev)
         self.ids = torch.zeros((n, self.cap), dtype=torch.int32, device=dev)
         self.mask = torch.zeros((n, MASK_BYTES), dtype=torch.uint8, device=dev) if with_mask else None
-        self.offsets = torch.zeros(n + 1, dtype=torch.int32, device=dev)
-        self.values = torch.zeros(n * self.cap, dtype=torch.int32, device=dev)
         self.csr_scratch = torch.zeros(max(1, N.lib().jq_csr_scratch_ints(n)), dtype=torch.int32, device=dev)
         self.actions = torch.full((n,), -1, dtype=torch.int32, device=dev)
         self.compact_actions = torch.full((n,), -1, dtype=torch.int32, device=dev)
@@ -153,6 +163,11 @@ class JunqiEnvB200:
         N.check(N.lib().jq_legal_slots(ctypes.byref(self.batch.struct), self._ptr(s), out.data_ptr(),
                                        _stream_ptr()), "jq_legal_slots")
         return out
+
+    def io_prefix_bytes(self, values: int) -> int:
+        """Bytes of ``io`` that hold the step results, the CSR offsets and the
+        first ``values`` CSR values."""
+        return self.values_byte_offset + 4 * min(int(values), self.n * self.cap)
 
     def csr(self):
         """(offsets (N+1,), values (N*cap,)) of the last legal generation."""

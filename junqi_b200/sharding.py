@@ -70,6 +70,45 @@ def sum_over_ranks(value: int, device: torch.device | str = "cpu") -> int:
     return int(t.item())
 
 
+def core_slice(cores: list[int], local_rank: int, local_world: int) -> list[int]:
+    """The host cores of ``local_rank`` when the node's ``cores`` are split
+    into ``local_world`` disjoint, contiguous shares (differing by at most
+    one core).  With fewer cores than ranks, ranks share cores round-robin."""
+    if local_world <= 0 or not 0 <= local_rank < local_world:
+        raise ValueError(f"bad local rank {local_rank} for {local_world} ranks per node")
+    cores = sorted(int(c) for c in cores)
+    if not cores:
+        raise ValueError("no host cores given")
+    if len(cores) < local_world:
+        return [cores[local_rank % len(cores)]]
+    base, extra = divmod(len(cores), local_world)
+    start = local_rank * base + min(local_rank, extra)
+    return cores[start:start + base + (1 if local_rank < extra else 0)]
+
+
+def pin_rank_cores(local_rank: int, local_world: int) -> list[int]:
+    """Restrict this process to its share of the cores it may run on, so
+    ranks of one node do not contend for the host threads that feed their
+    GPUs; returns the cores kept (all of them where affinity is not
+    supported)."""
+    import os
+    if not hasattr(os, "sched_getaffinity"):
+        return []
+    mine = core_slice(sorted(os.sched_getaffinity(0)), local_rank, local_world)
+    os.sched_setaffinity(0, mine)
+    return mine
+
+
+def gather_over_ranks(obj) -> list:
+    """Every rank's ``obj`` (a small picklable record), in rank order, on
+    every rank; ``[obj]`` without a process group."""
+    if _world() == 1:
+        return [obj]
+    out = [None] * _world()
+    dist.all_gather_object(out, obj)
+    return out
+
+
 def stats_dict(stats: torch.Tensor) -> dict[str, int]:
     vals = stats.detach().cpu().tolist()
     return dict(zip(STAT_NAMES, (int(v) for v in vals)))

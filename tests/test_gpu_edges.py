@@ -218,3 +218,24 @@ def test_each_env_resets_from_its_own_pool():
         lineup = pa[L.jq_pool_index(10, 0, e, pa.shape[0])]
         assert np.array_equal(got[e], np.where(lineup != 0, lineup, -1))
     del junk
+
+
+def test_io_buffer_prefix_holds_results_and_csr():
+    """env.io lays out the step results, the CSR offsets and the CSR values
+    in that order: one host copy of io_prefix_bytes(total) reads them all."""
+    env = JunqiEnvB200(37, pool=tables.build_setup_pool(8, seed=3), with_obs=False)
+    env.reset(seed=2)
+    for t in range(1, 6):
+        env.ply(env.sample_uniform(2, t), seed=2, ply=t)
+    off, val = env.csr()
+    tot = int(off[-1].item())
+    host = env.io[: env.io_prefix_bytes(tot)].cpu().numpy()
+    base = env.io.data_ptr()
+    for k, v in env.out.items():
+        o = v.data_ptr() - base
+        assert o % 16 == 0
+        got = host[o:o + v.numel() * v.element_size()].view(v.cpu().numpy().dtype)
+        assert np.array_equal(got, v.cpu().numpy()), k
+    o = off.data_ptr() - base
+    assert np.array_equal(host[o:o + 4 * (env.n + 1)].view(np.int32), off.cpu().numpy())
+    assert np.array_equal(host[env.values_byte_offset:].view(np.int32), val[:tot].cpu().numpy())

@@ -69,7 +69,8 @@ def _rank_main(rank: int, world: int, port: int, q) -> None:
         sharding.reduce_episode_stats(t)
         ms = sharding.max_over_ranks(10.0 + rank)
         tot = sharding.sum_over_ranks(applied)
-        q.put((rank, t.numpy().tolist(), ms, tot, applied))
+        recs = sharding.gather_over_ranks({"rank": rank, "applied": applied})
+        q.put((rank, t.numpy().tolist(), ms, tot, applied, recs))
     finally:
         dist.destroy_process_group()
 
@@ -110,7 +111,20 @@ def test_two_gloo_ranks_reduce_episode_stats_of_independent_slices():
         expect_stats += s
         expect_tot += a
     assert expect_stats[3] > 0, "the rollout must finish some episodes"
-    for rank, stats, ms, tot, applied in got:
+    for rank, stats, ms, tot, applied, recs in got:
         assert stats == expect_stats.tolist(), f"rank {rank}"
         assert ms == 11.0
         assert tot == expect_tot
+        assert [r["rank"] for r in recs] == [0, 1] and sum(r["applied"] for r in recs) == expect_tot
+
+
+def test_core_slices_are_disjoint_and_cover_the_node():
+    cores = [0, 1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12, 13, 14, 15, 16]
+    for world in (1, 2, 4, 8):
+        parts = [sharding.core_slice(cores, r, world) for r in range(world)]
+        assert sorted(c for p in parts for c in p) == cores
+        assert max(map(len, parts)) - min(map(len, parts)) <= 1
+    assert sharding.core_slice([3, 1], 2, 4) == [1]  # fewer cores than ranks: shared round-robin
+    assert sharding.gather_over_ranks({"a": 1}) == [{"a": 1}]
+    with pytest.raises(ValueError):
+        sharding.core_slice(cores, 2, 2)
