@@ -1,6 +1,6 @@
 """Parity at the benchmark's full sizes: sampled envs plus whole-batch properties.
 
-The oracle cannot replay 65,536 envs in seconds, so at BASELINE's full
+The oracle cannot replay 65,536 envs in seconds, so at the benchmark's full
 shapes every check is one of:
 
 * sampled parity -- at checkpoint plies a random sample of envs is copied to
@@ -13,8 +13,16 @@ shapes every check is one of:
   ascending, duplicate-free and sized like the mask rows; episode
   statistics add up.
 
-Shapes: configs[2] (65,536 envs, observations of all 4 seats, masked
-softmax) and configs[3] (32,768 envs per GPU, 512 plies, pool of 8,192).
+Shapes (the benchmark's configurations, GameState rules, HALF_DARK):
+
+* configs[1], the headline: 4,096 envs, acting-seat observation, uniform
+  policy, pool of 10,000, 1,000 plies;
+* configs[2]: 65,536 envs, observations of all 4 seats, masked softmax;
+* configs[3]: 32,768 envs, 512 plies, pool of 8,192, masked softmax;
+* 32,768 late-game starts (``workloads.late_game_starts``),
+  2,000 uniform plies.
+At every checkpoint the sampled envs' observations of their acting seat
+(of all four seats at configs[2]'s last checkpoint) are compared too.
 """
 from __future__ import annotations
 
@@ -85,20 +93,27 @@ def _free_bytes() -> int:
     return free
 
 
-@pytest.mark.parametrize("name,envs,seats,pool_n,plies,checks", [
-    ("configs[2]", 65536, 4, 10_000, 40, (1, 20, 40)),
-    ("configs[3]", 32768, 1, 8192, 512, (1, 256, 511)),
+@pytest.mark.parametrize("name,envs,seats,pool_n,plies,policy,late,checks", [
+    ("configs[1]", 4096, 1, 10_000, 1000, "uniform", False, (1, 250, 500, 750, 1000)),
+    ("configs[2]", 65536, 4, 10_000, 40, "softmax", False, (1, 20, 40)),
+    ("configs[3]", 32768, 1, 8192, 512, "softmax", False, (1, 256, 511)),
+    ("configs[4]", 32768, 1, 10_000, 2000, "uniform", True, (1, 700, 1400, 2000)),
 ])
-def test_full_size_rollout_sampled_parity(name, envs, seats, pool_n, plies, checks):
-    seed = 900 + envs // 4096
+def test_full_size_rollout_sampled_parity(name, envs, seats, pool_n, plies, policy, late, checks):
+    seed = 900 + envs // 4096 + 7 * late
     pool = tables.build_setup_pool(pool_n, seed=seed)
-    env = JunqiEnvB200(envs, show_mode=HALF_DARK, pool=pool, obs_seats=seats, with_obs=False,
+    env = JunqiEnvB200(envs, show_mode=HALF_DARK, pool=pool, obs_seats=seats, with_obs=seats == 1,
                        rules=N.RULES_GAMESTATE)
     L = N.lib()
     rng = np.random.default_rng(seed)
-    env.reset(seed=seed)
+    if late:
+        from junqi_b200.workloads import late_game_starts
+        late_game_starts(env, seed)
+    else:
+        env.reset(seed=seed)
+    sampler = env.sample_uniform if policy == "uniform" else env.sample_softmax
     for t in range(1, plies + 1):
-        acts = env.sample_softmax(seed, t)
+        acts = sampler(seed, t)
         if t not in checks:
             env.ply(acts, seed=seed, ply=t)
             continue
@@ -115,6 +130,15 @@ def test_full_size_rollout_sampled_parity(name, envs, seats, pool_n, plies, chec
         _check_state(env, orc, idx, t)
         _check_legal(env, orc, idx, t)
         _check_properties(env, t)
+        if seats == 1:  # the acting seat's observation, as the benchmark's ply loop builds it
+            sp, gl = env.observe()
+            osp, ogl = orc.obs()
+            got_sp = sp[torch.from_numpy(idx).to(sp.device)].cpu().numpy()
+            got_gl = gl[torch.from_numpy(idx).to(gl.device)].cpu().numpy()
+            bad = [int(idx[i]) for i in range(len(idx))
+                   if not np.array_equal(got_sp[i].view(np.uint32), osp[i].view(np.uint32))
+                   or not np.array_equal(got_gl[i].view(np.uint32), ogl[i].view(np.uint32))]
+            assert not bad, f"{name} ply {t}: acting-seat observation differs in envs {bad[:6]}"
         if seats == 4 and t == checks[-1]:
             need = envs * 4 * (317 * 289 * 4 + 28 * 4)
             if _free_bytes() < need + (4 << 30):
@@ -130,4 +154,6 @@ def test_full_size_rollout_sampled_parity(name, envs, seats, pool_n, plies, chec
             del sp, gl
             env.spatial = env.global_ = None
             torch.cuda.empty_cache()
-    assert int(env.stats[3]) >= 0
+    s = env.stats.cpu().numpy()
+    if plies >= 1000:  # long rollouts finish games and reset them from the pool
+        assert s[3] > 0, f"{name}: no episode finished in {plies} plies"
