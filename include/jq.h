@@ -355,6 +355,14 @@ int jq_sample_softmax(const jq_batch *b, const int32_t *d_counts, const int32_t 
                       int32_t cap, uint64_t seed, uint64_t ply, int32_t *d_compact_actions,
                       int32_t *d_world_actions, void *stream);
 
+/* Per-CTA timestamps of the last obs_kernel (kernel 0) or rules_kernel
+ * (kernel 1) launch: `ctas` rows of 8 uint64 (globaltimer ns at fixed points
+ * of the kernel; see junqi_b200/csrc/jq_trace.cuh), copied to host memory.
+ * Available only in the tracing build of the library (libjq_trace.so, `make
+ * trace`); the normal build returns JQ_ERR_NOT_READY.  A profiling aid with no
+ * counterpart in the reference. */
+int jq_trace_read(int32_t kernel, uint64_t *host, int32_t ctas);
+
 #ifdef __cplusplus
 }
 #endif

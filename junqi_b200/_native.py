@@ -12,6 +12,7 @@ from pathlib import Path
 
 _PKG = Path(__file__).resolve().parent
 LIB_PATH = _PKG / "libjq.so"
+TRACE_LIB_PATH = _PKG / "libjq_trace.so"  # the same library with kernel timestamps (make -C csrc trace)
 CSRC = _PKG / "csrc"
 
 JQ_OK = 0
@@ -91,29 +92,42 @@ SIGNATURES = {
     "jq_cell_beliefs_update": (ctypes.c_int, [_PB, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "jq_sample_uniform": (ctypes.c_int, [_i32, _vp, _vp, _i32, _u64, _u64, _vp, _vp]),
     "jq_sample_softmax": (ctypes.c_int, [_PB, _vp, _vp, _i32, _u64, _u64, _vp, _vp, _vp]),
+    "jq_trace_read": (ctypes.c_int, [_i32, _vp, _i32]),
 }
 
 
-def build(force: bool = False) -> Path:
-    """Compile libjq.so for sm_100a with nvcc (csrc/Makefile)."""
+def build(force: bool = False, trace: bool = False) -> Path:
+    """Compile libjq.so (or, with ``trace``, libjq_trace.so) for sm_100a with
+    nvcc (csrc/Makefile)."""
+    path = TRACE_LIB_PATH if trace else LIB_PATH
     srcs = list(CSRC.glob("*.cu")) + list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.h")) + \
         [_PKG.parent / "include" / "jq.h"]
-    stale = not LIB_PATH.exists() or any(p.stat().st_mtime > LIB_PATH.stat().st_mtime for p in srcs)
+    stale = not path.exists() or any(p.stat().st_mtime > path.stat().st_mtime for p in srcs)
     if force or stale:
-        subprocess.run(["make", "-s", "-C", str(CSRC)], check=True)
-    return LIB_PATH
+        subprocess.run(["make", "-s", "-C", str(CSRC)] + (["trace"] if trace else []), check=True)
+    return path
 
 
 _lib = None
+_lib_path = LIB_PATH
+
+
+def use_trace_library() -> None:
+    """Load libjq_trace.so instead of libjq.so (before the first call into
+    the library): the same kernels plus per-CTA timestamps (jq_trace_read)."""
+    global _lib_path
+    if _lib is not None and _lib_path != TRACE_LIB_PATH:
+        raise RuntimeError("libjq.so is already loaded in this process")
+    _lib_path = TRACE_LIB_PATH
 
 
 def lib():
     """Load libjq.so (raising if it is absent) and declare every signature."""
     global _lib
     if _lib is None:
-        if not LIB_PATH.exists():
-            raise RuntimeError(f"libjq.so not built at {LIB_PATH}; run junqi_b200._native.build()")
-        L = ctypes.CDLL(str(LIB_PATH))
+        if not _lib_path.exists():
+            raise RuntimeError(f"{_lib_path.name} not built at {_lib_path}; run junqi_b200._native.build()")
+        L = ctypes.CDLL(str(_lib_path))
         for name, (res, args) in SIGNATURES.items():
             fn = getattr(L, name)
             fn.restype = res

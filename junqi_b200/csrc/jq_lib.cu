@@ -693,6 +693,21 @@ int jq_csr_noalloc(int32_t n, const int32_t *d_counts, const int32_t *d_ids, int
     return launch_csr(n, d_counts, d_ids, cap, scratch, d_offsets, d_values, (cudaStream_t)stream);
 }
 
+// Per-CTA timestamps of the last obs_kernel / rules_kernel launch, in the
+// tracing build only (JQ_TRACE, `make trace`).
+int jq_trace_read(int32_t kernel, uint64_t *host, int32_t ctas) {
+#ifdef JQ_TRACE
+    if (kernel < 0 || kernel >= TRACE_KERNELS || !host || ctas <= 0 || ctas > TRACE_CTAS)
+        return fail(JQ_ERR_ARG, "jq_trace_read: bad kernel index, output or CTA count");
+    CU(cudaMemcpyFromSymbol(host, g_trace, sizeof(uint64_t) * TRACE_POINTS * ctas,
+                            sizeof(uint64_t) * TRACE_POINTS * TRACE_CTAS * kernel));
+    return JQ_OK;
+#else
+    (void)kernel, (void)host, (void)ctas;
+    return fail(JQ_ERR_NOT_READY, "libjq was built without JQ_TRACE (make trace builds libjq_trace.so)");
+#endif
+}
+
 static int observe_launch(const jq_batch *b, const int8_t *d_observers, int32_t seats_per_env, int32_t show_mode,
                           const float *d_beliefs, float *d_spatial, float *d_global, void *stream) {
     int rc = check_batch(b);

@@ -43,6 +43,7 @@
 // that pass 2 overwrites the zeros pass 1 left at value-carrying floats.
 #pragma once
 #include "jq_rules.cuh"
+#include "jq_trace.cuh"
 
 namespace jq {
 
@@ -542,6 +543,7 @@ __global__ void __launch_bounds__(OBS_THREADS, OBS_MIN_CTAS) obs_kernel(jq_batch
     extern __shared__ __align__(16) unsigned char smem_raw[];
     ObsSmem &S = *reinterpret_cast<ObsSmem *>(smem_raw);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid == 0) JQ_TRACE_AT(0, TO_ENTRY);
     asm volatile("griddepcontrol.launch_dependents;");
     // once per CTA: observer rotations, belief tables and board-static words
     // into shared memory; both bitstreams cleared
@@ -556,6 +558,7 @@ __global__ void __launch_bounds__(OBS_THREADS, OBS_MIN_CTAS) obs_kernel(jq_batch
     // memory -- tickets, state, outputs -- only after the previous kernel
     asm volatile("griddepcontrol.wait;" ::: "memory");
     __syncthreads();
+    if (tid == 0) JQ_TRACE_AT(0, TO_WAITED);
     const int units = b.n * seats;
     if (warp < OBS_STREAM_WARPS) {
         for (int k = 0;; ++k) {
@@ -563,8 +566,10 @@ __global__ void __launch_bounds__(OBS_THREADS, OBS_MIN_CTAS) obs_kernel(jq_batch
             bar_sync(BAR_FULL0 + bi, OBS_THREADS);  // buffer bi staged
             UnitBuf &B = S.buf[bi];
             if (B.u < 0) break;
+            if (k == 0 && tid == 0) JQ_TRACE_AT(0, TO_FIRST_STREAM);
             stream_unit(B, S.prior, S.uniform, ext_bel != nullptr, spatial, global, warp, lane, OBS_STREAM_WARPS,
                         BAR_STREAM);
+            if (tid == 0) JQ_TRACE_AT(0, TO_LAST_STREAMED);
             bar_arrive(BAR_EMPTY0 + bi, OBS_THREADS);  // buffer bi free again
         }
     } else {
@@ -593,6 +598,7 @@ __global__ void __launch_bounds__(OBS_THREADS, OBS_MIN_CTAS) obs_kernel(jq_batch
             }
             stage_unit(b, seats, mode, ext_bel, global, S, B, u, o, unit_head(spatial, u), t, BAR_STAGE);
             bar_sync(BAR_STAGE, OBS_STAGE_THREADS);    // unit staged by every staging thread
+            if (k == 0 && t == 0) JQ_TRACE_AT(0, TO_FIRST_STAGED);
             bar_arrive(BAR_FULL0 + bi, OBS_THREADS);  // hand it to the streaming warps
             if (t == 0) {
                 const int un = atomicAdd(&ticket[0], 1);
@@ -605,6 +611,8 @@ __global__ void __launch_bounds__(OBS_THREADS, OBS_MIN_CTAS) obs_kernel(jq_batch
         }
         if (k >= 1) bar_sync(BAR_EMPTY0 + ((k - 1) & 1), OBS_THREADS);  // the last unit has been streamed
         if (t == 0) {
+            JQ_TRACE_AT(0, TO_EXIT);
+            JQ_TRACE_COUNT(0, TO_UNITS, k);
             __threadfence();
             if (atomicAdd(&ticket[1], 1) == (int)gridDim.x - 1) {
                 ticket[0] = 0;

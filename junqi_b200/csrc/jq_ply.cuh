@@ -2,6 +2,7 @@
 // work), and the rules kernel itself.
 #pragma once
 #include "jq_rules.cuh"
+#include "jq_trace.cuh"
 
 namespace jq {
 
@@ -87,6 +88,7 @@ __device__ bool warp_ply_env(const RuleArgs &a, const Topo &T, WEnv &w, int e, i
 __global__ void __launch_bounds__(RULE_THREADS, 4) rules_kernel(RuleArgs a) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     RuleSmem &S = *reinterpret_cast<RuleSmem *>(smem_raw);
+    if (threadIdx.x == 0) JQ_TRACE_AT(1, TR_ENTRY);
     // launched as a programmatic dependent: the next kernel may start its
     // own table loads now; state is touched only after the previous kernel
     // in the stream has completed
@@ -95,6 +97,7 @@ __global__ void __launch_bounds__(RULE_THREADS, 4) rules_kernel(RuleArgs a) {
     if (threadIdx.x == 0) S.applied = 0;
     asm volatile("griddepcontrol.wait;" ::: "memory");
     __syncthreads();
+    if (threadIdx.x == 0) JQ_TRACE_AT(1, TR_WAITED);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     WEnv &w = S.w[warp];
     for (int e = blockIdx.x * RULE_WARPS + warp; e < a.b.n; e += gridDim.x * RULE_WARPS) {
@@ -102,6 +105,7 @@ __global__ void __launch_bounds__(RULE_THREADS, 4) rules_kernel(RuleArgs a) {
         if (applied && lane == 0 && a.stats) atomicAdd_block(&S.applied, 1);
     }
     __syncthreads();
+    if (threadIdx.x == 0) JQ_TRACE_AT(1, TR_EXIT);
     if (threadIdx.x == 0 && a.stats && S.applied) atomicAdd((unsigned long long *)&a.stats[5], (unsigned long long)S.applied);
 }
 

@@ -1,0 +1,49 @@
+// jq_trace.cuh -- optional per-CTA timestamps of the hot kernels.
+//
+// Built only into the tracing variant of the library (`make trace`, which
+// defines JQ_TRACE and writes libjq_trace.so); in the normal build every
+// JQ_TRACE_AT is empty and the kernels are unchanged.  With tracing, one
+// thread per CTA stores the %globaltimer value (ns) of a few points of the
+// kernel into g_trace[kernel][cta][point]; jq_trace_read copies the table of
+// the last launch of each kernel to the host (junqi_b200/trace.py turns it
+// into a timeline).
+#pragma once
+#include <stdint.h>
+
+namespace jq {
+
+constexpr int TRACE_KERNELS = 2;   // 0: obs_kernel, 1: rules_kernel
+constexpr int TRACE_CTAS = 1024;   // CTAs recorded per launch (grid beyond this is not traced)
+constexpr int TRACE_POINTS = 8;
+
+// obs_kernel points
+enum : int { TO_ENTRY = 0, TO_WAITED = 1, TO_FIRST_STAGED = 2, TO_FIRST_STREAM = 3, TO_LAST_STREAMED = 4,
+             TO_EXIT = 5, TO_UNITS = 6 };
+// rules_kernel points
+enum : int { TR_ENTRY = 0, TR_WAITED = 1, TR_EXIT = 2, TR_ENVS = 3 };
+
+#ifdef JQ_TRACE
+__device__ uint64_t g_trace[TRACE_KERNELS][TRACE_CTAS][TRACE_POINTS];
+__device__ __forceinline__ uint64_t trace_clock() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+#define JQ_TRACE_AT(kernel, point)                                                          \
+    do {                                                                                    \
+        if (blockIdx.x < TRACE_CTAS) g_trace[kernel][blockIdx.x][point] = trace_clock();     \
+    } while (0)
+#define JQ_TRACE_COUNT(kernel, point, value)                                                \
+    do {                                                                                    \
+        if (blockIdx.x < TRACE_CTAS) g_trace[kernel][blockIdx.x][point] = (uint64_t)(value); \
+    } while (0)
+#else
+#define JQ_TRACE_AT(kernel, point) \
+    do {                           \
+    } while (0)
+#define JQ_TRACE_COUNT(kernel, point, value) \
+    do {                                     \
+    } while (0)
+#endif
+
+}  // namespace jq

@@ -1,0 +1,89 @@
+"""Per-CTA timelines of the observation and rules kernels (tracing build).
+
+    python -m junqi_b200.trace [--envs 4096] [--plies 200]
+
+builds libjq_trace.so (the library compiled with JQ_TRACE: one %globaltimer
+store per CTA at a few points of each kernel, jq_trace.cuh), plays a
+configs[1]-style rollout (acting-seat observation, uniform policy, GameState
+rules) and prints, for the last ply's observation and rules launches, where
+their time goes: CTA start spread, wait for the previous kernel, the first
+unit's staging before any store, the streaming span and the tail.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+
+import numpy as np
+
+from . import _native as N
+
+OBS, RULES = 0, 1
+
+
+def read(kernel: int, ctas: int) -> np.ndarray:
+    """(ctas, 8) uint64 timestamps of the last launch of `kernel`."""
+    out = np.zeros((ctas, 8), np.uint64)
+    N.check(N.lib().jq_trace_read(kernel, out.ctypes.data, ctas), "jq_trace_read")
+    return out
+
+
+def obs_timeline(t: np.ndarray) -> dict:
+    """Observation-kernel phases in microseconds from the first CTA's entry."""
+    t = t.astype(np.int64)
+    t0 = t[:, 0].min()
+    us = lambda a: (a - t0) / 1e3  # noqa: E731
+    end = t[:, 5].max()
+    return {"ctas": int(len(t)), "span_us": (end - t0) / 1e3,
+            "entry_spread_us": float(us(t[:, 0]).max()),
+            "waited_us_median": float(np.median(us(t[:, 1]))),
+            "first_staged_us_median": float(np.median(us(t[:, 2]))),
+            "first_stream_us_median": float(np.median(us(t[:, 3]))),
+            "first_stream_us_max": float(us(t[:, 3]).max()),
+            "last_streamed_us_min": float(us(t[:, 4]).min()),
+            "last_streamed_us_median": float(np.median(us(t[:, 4]))),
+            "exit_us_min": float(us(t[:, 5]).min()), "exit_us_max": float(us(t[:, 5]).max()),
+            "units_per_cta_min": int(t[:, 6].min()), "units_per_cta_max": int(t[:, 6].max())}
+
+
+def rules_timeline(t: np.ndarray) -> dict:
+    t = t.astype(np.int64)
+    t0 = t[:, 0].min()
+    us = lambda a: (a - t0) / 1e3  # noqa: E731
+    return {"ctas": int(len(t)), "span_us": float(us(t[:, 2]).max()),
+            "waited_us_median": float(np.median(us(t[:, 1]))),
+            "exit_us_min": float(us(t[:, 2]).min()), "exit_us_median": float(np.median(us(t[:, 2]))),
+            "exit_us_p90": float(np.percentile(us(t[:, 2]), 90)), "exit_us_max": float(us(t[:, 2]).max())}
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--envs", type=int, default=4096)
+    ap.add_argument("--plies", type=int, default=200)
+    args = ap.parse_args()
+    N.build(trace=True)
+    N.use_trace_library()
+    import torch
+
+    from . import tables
+    from .env import JunqiEnvB200
+    env = JunqiEnvB200(args.envs, pool=tables.build_setup_pool(10_000, seed=42), rules=N.RULES_GAMESTATE)
+    env.reset(seed=7)
+    for t in range(1, args.plies + 1):
+        env.observe()
+        env.ply(env.sample_uniform(7, t), seed=7, ply=t)
+    torch.cuda.synchronize()
+    env.observe()
+    torch.cuda.synchronize()
+    st = N.lib()
+    dev = torch.cuda.current_device()
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    obs_ctas = min(2 * sms, args.envs)
+    rule_ctas = min((args.envs + 7) // 8, 1024)
+    print(json.dumps({"kernel": "obs_kernel", "units": args.envs, **obs_timeline(read(OBS, obs_ctas))}))
+    print(json.dumps({"kernel": "rules_kernel", "envs": args.envs, **rules_timeline(read(RULES, rule_ctas))}))
+    del st
+
+
+if __name__ == "__main__":
+    main()
