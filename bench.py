@@ -220,6 +220,101 @@ def reference_arm(args, cfg: dict) -> None:
     print(json.dumps(line), flush=True)
 
 
+def _junqi_core_worker(rank: int, envs: int, burn_in: int, budget_s: float, seed: int, q) -> None:
+    """One host core's slice: the reference's own CPU path for one ply of the
+    single-env rules (the JunqiEnv ply, GameState.step, state.py:626):
+    acting-seat observation (ObservationBuilder.build_into, observation.py:
+    510), legal ids, a uniform action, the step and the four seats'
+    BeliefTensor.update (info_model.py:271), with finished games reset from
+    seeded setups (GameState.new_game, setup.py:162 lineups)."""
+    import random
+    sys.path.insert(0, str(ROOT / "baseline" / "_ref"))
+    from junqi_core.info_model import BeliefTensor
+    from junqi_core.observation import ObservationBuilder
+    from junqi_core.rules import Seat
+    from junqi_core.setup import generate_random_setup
+    from junqi_core.state import Action, GameState
+    rng = random.Random(seed + 7919 * rank)
+
+    def fresh():
+        g = GameState.new_game(generate_random_setup(random.Random(rng.getrandbits(32))))
+        return g, [BeliefTensor.initial(g, Seat(k)) for k in range(4)]
+
+    games = [fresh() for _ in range(envs)]
+    builder = ObservationBuilder()
+    sp = np.zeros((317, 17, 17), np.float32)
+    gl = np.zeros(28, np.float32)
+
+    def ply(obs: bool) -> int:
+        done = 0
+        for i, (g, bel) in enumerate(games):
+            if obs:
+                builder.build_into(g, bel[g.turn.value], g.turn, sp, gl)
+            ids = g.legal_action_ids()
+            if g.terminated or len(ids) == 0:
+                games[i] = fresh()
+                continue
+            a = int(ids[rng.randrange(len(ids))])
+            sf, df = a // 289, a % 289
+            new, mr = g.step(Action(seat=g.turn, src=(sf % 17, sf // 17), dst=(df % 17, df // 17)))
+            for b in bel:
+                b.update(g, new, mr)
+            games[i] = (new, bel) if not new.terminated else fresh()
+            done += 1
+        return done
+
+    for _ in range(burn_in):
+        ply(False)
+    done, plies = 0, 0
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < budget_s:
+        done += ply(True)
+        plies += 1
+    q.put((done, time.perf_counter() - t0, plies))
+
+
+def reference_python_arm(args, cfg: dict) -> None:
+    """The reference's own Python implementation of the path (junqi_core,
+    staged into baseline/_ref by baseline/build_ref_cuda.py), timed on all
+    host cores, one process per core each playing its own slice of envs:
+    a reported baseline beside the oracle port of --impl reference."""
+    import multiprocessing as mp
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    if not (ROOT / "baseline" / "_ref" / "junqi_core").exists():
+        print(json.dumps({"impl": "reference-python", "unavailable": "baseline/_ref has no junqi_core; run "
+                          "baseline/build_ref_cuda.py where the reference checkout exists"}), flush=True)
+        return
+    if cfg["seats"] != 1:
+        print(json.dumps({"impl": "reference-python", "unavailable": "only the acting-seat configs are timed"}))
+        return
+    cores = host_cores()
+    per = 8
+    burn = min(args.burn_in, 50)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_junqi_core_worker, args=(r, per, burn, 20.0, args.seed, q)) for r in range(cores)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=600) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    done = sum(r[0] for r in res)
+    secs = max(r[1] for r in res)
+    rate = done / secs
+    sample = (f"{cores} processes x {per} envs, {min(r[2] for r in res)}-{max(r[2] for r in res)} plies each after "
+              f"a {burn}-ply burn-in, acting-seat observation + legal ids + step + 4-seat belief update, "
+              f"{secs:.1f} s")
+    print(json.dumps({"impl": "reference-python", "metric": "env plies/s (step + legal mask + 317-ch obs)",
+                      "value": rate, "unit": "plies/s", "n_gpus": 1, "higher_is_better": True,
+                      "config": arm_config(cfg, args, 1),
+                      "cpu_baseline": {"value": rate, "unit": "plies/s", "cores": cores, "kind": "reference",
+                                       "sample": sample},
+                      "source": "junqi_core (GameState.step, ObservationBuilder.build_into, BeliefTensor.update) "
+                                "from baseline/_ref"}), flush=True)
+
+
 def reference_cuda_arm(args, cfg: dict) -> None:
     """The reference's own CUDA extension on this GPU -- a reported baseline,
     not part of the driver contract.  Built by baseline/build_ref_cuda.py
@@ -312,7 +407,7 @@ def main() -> None:
     ap.add_argument("--burn-in", type=int, default=200,
                     help="untimed plies played before the warm-up, so the timed plies sample a rollout's steady "
                          "mix of openings, combat, finished games and resets rather than only fresh games")
-    ap.add_argument("--impl", default="b200", choices=["b200", "reference", "reference-cuda"])
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference", "reference-cuda", "reference-python"])
     ap.add_argument("--config", default="cfg2", choices=sorted(CONFIGS))
     ap.add_argument("--envs", type=int, default=None, help="envs per GPU (default: the config's)")
     ap.add_argument("--e2e-steps", type=int, default=100)
@@ -332,6 +427,9 @@ def main() -> None:
         args.steps = cfg["plies"]
     if args.impl == "reference-cuda":
         reference_cuda_arm(args, cfg)
+        return
+    if args.impl == "reference-python":
+        reference_python_arm(args, cfg)
         return
     if args.impl == "reference":
         reference_arm(args, cfg)

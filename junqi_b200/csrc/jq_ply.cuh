@@ -53,7 +53,9 @@ __device__ __forceinline__ void stage_topo(Topo &dst_t, int tid, int nthreads) {
 __device__ bool warp_ply_env(const RuleArgs &a, const Topo &T, WEnv &w, int e, int lane) {
     const jq_batch &b = a.b;
     bool applied = false;
+    const bool traced = threadIdx.x == 0 && e < RULE_WARPS * (int)gridDim.x;  // warp 0's first env
     warp_load(b, T, w, e, lane, (a.flags & DO_STEP) != 0);
+    if (traced) JQ_TRACE_AT(1, TR_LOADED);
     if (a.flags & DO_BELIEF_INIT) {
         warp_belief_init(b, T, w, e, lane, a.mode);
         b.hist_src[(size_t)e * HIST + lane] = -1;
@@ -62,6 +64,7 @@ __device__ bool warp_ply_env(const RuleArgs &a, const Topo &T, WEnv &w, int e, i
         __syncwarp();
     }
     if (a.flags & DO_STEP) applied = warp_step(b, T, w, e, lane, a.acts[e], a.mode, a.out, a.stats);
+    if (traced) JQ_TRACE_AT(1, TR_STEPPED);
     if ((a.flags & DO_RESET) && a.pool && a.pool_size > 0) {
         int row = -1;
         if (a.rows) {
@@ -73,15 +76,17 @@ __device__ bool warp_ply_env(const RuleArgs &a, const Topo &T, WEnv &w, int e, i
         if (row >= 0) warp_reset(b, T, w, e, lane, a.pool + (size_t)row * NP, a.mode);
     }
     __syncwarp();
+    if (traced) JQ_TRACE_AT(1, TR_RESET);
     if (a.flags & DO_LEGAL) {
         int seat = a.seats ? a.seats[e] : b.turn[e];
         const bool skip = seat < 0 || seat > 3 || b.terminated[e] || w.sdead[seat & 3];
         seat &= 3;
         const int cnt = warp_legal(T, w, lane, seat, skip, a.ids ? a.ids + (size_t)e * a.cap : nullptr, a.cap,
-                                   a.mask ? a.mask + (size_t)e * MASK_BYTES : nullptr);
+                                   a.mask ? a.mask + (size_t)e * MASK_BYTES : nullptr, traced);
         if (lane == 0 && a.counts) a.counts[e] = cnt;
     }
     __syncwarp();
+    if (traced) JQ_TRACE_AT(1, TR_MASKED);
     return applied;
 }
 

@@ -19,6 +19,7 @@
 // expansion over per-cell rail-neighbour masks).
 #pragma once
 #include "jq_common.cuh"
+#include "jq_trace.cuh"
 
 namespace jq {
 
@@ -64,6 +65,8 @@ constexpr int CBW = (MASK_BYTES + 31) / 32 + 1;
 struct __align__(16) WEnv {
     uint32_t cbits[CBW];     // the canonical mask as one row-major bitstream (bit j = mask byte j)
     alignas(16) uint8_t bel[4 * NP];  // belief codes (observer-major), loaded with the state for a step
+    int16_t rem[4 * 4 * 12];  // enemy inventories (observer, seat, type), loaded when a ply changes them
+    uint8_t rtr[16];          // their tracked flags (observer, seat)
     uint64_t cmv[4][4];      // V's combat-memory sets per observer: direct lo/hi, chain lo/hi
     int32_t scan[32];
     StepCtx x;
@@ -311,7 +314,7 @@ __device__ __forceinline__ uint4 mask_chunk(const WEnv &w, int j0) {
 // (up to cap); optional canonical (16641) byte mask.  Returns the count on
 // every lane.
 __device__ int warp_legal(const Topo &T, WEnv &w, int lane, int seat, bool skip, int32_t *ids, int cap,
-                          uint8_t *mask_env) {
+                          uint8_t *mask_env, bool traced = false) {
     uint32_t empty[NW], land[NW], d[NW] = {0, 0, 0, 0, 0};
     board_masks(T, w, lane, seat & 1, empty, land);
     int src = skip ? -1 : lane_source(w, lane, seat);
@@ -355,6 +358,7 @@ __device__ int warp_legal(const Topo &T, WEnv &w, int lane, int seat, bool skip,
             }
         }
     }
+    if (traced) JQ_TRACE_AT(1, TR_IDS);
     if (mask_env) {
         for (int k = lane; k < CBW; k += 32) w.cbits[k] = 0u;
         __syncwarp();
@@ -618,17 +622,26 @@ __device__ void warp_belief_init(const jq_batch &b, const Topo &T, WEnv &w, int 
     }
 }
 
-__device__ __forceinline__ void rem_dec(const jq_batch &b, int e, int o, int seat, int ti) {
-    if (seat < 0 || seat > 3 || ti < 0) return;
-    size_t tr = (size_t)e * 16 + o * 4 + seat;
-    if (!b.rem_tracked[tr]) return;
-    int16_t *r = &b.remaining[tr * 12 + ti];
-    if (*r > 0) *r = (int16_t)(*r - 1);
+// Inventory rules on the env's shared-memory copy (observer o's rows only,
+// so lanes 0..3 never touch each other's entries); returns whether it changed.
+__device__ __forceinline__ bool rem_dec(WEnv &w, int o, int seat, int ti) {
+    if (seat < 0 || seat > 3 || ti < 0) return false;
+    const int tr = o * 4 + seat;
+    if (!w.rtr[tr]) return false;
+    int16_t &r = w.rem[tr * 12 + ti];
+    if (r <= 0) return false;
+    r = (int16_t)(r - 1);
+    return true;
 }
-__device__ __forceinline__ void rem_untrack(const jq_batch &b, int e, int o, int seat) {
-    size_t tr = (size_t)e * 16 + o * 4 + seat;
-    b.rem_tracked[tr] = 0;
-    for (int t = 0; t < 12; ++t) b.remaining[tr * 12 + t] = 0;
+__device__ __forceinline__ bool rem_untrack(WEnv &w, int o, int seat) {
+    const int tr = o * 4 + seat;
+    bool changed = w.rtr[tr] != 0;
+    w.rtr[tr] = 0;
+    for (int t = 0; t < 12; ++t) {
+        changed |= w.rem[tr * 12 + t] != 0;
+        w.rem[tr * 12 + t] = 0;
+    }
+    return changed;
 }
 
 // Lane o (0..3) applies R3, R5/R7, R4/R6, R1 and R9 for observer o; then the
@@ -637,21 +650,32 @@ __device__ __forceinline__ void rem_untrack(const jq_batch &b, int e, int o, int
 __device__ void warp_belief_update(const jq_batch &b, const Topo &T, WEnv &w, int e, int lane,
                                    const StepCtx &x, int mode, const int *died) {
     bool touched = false;  // R-rules rewrote a code of this lane's observer
+    bool inv = false;      // ... or an inventory entry
+    // Only combat plies and seat deaths change inventories: then the env's
+    // 192 entries and 16 tracked flags come into shared memory in one round
+    // trip, the rules run there, and the rows are written back once.
+    const bool inv_ply = x.combat || died[0] || died[1] || died[2] || died[3];
+    if (inv_ply) {
+#pragma unroll
+        for (int i = 0; i < 4 * 4 * 12 / 32; ++i) w.rem[lane + 32 * i] = b.remaining[(size_t)e * 192 + lane + 32 * i];
+        if (lane < 16) w.rtr[lane] = b.rem_tracked[(size_t)e * 16 + lane];
+        __syncwarp();
+    }
     if (lane < 4) {
         int o = lane;
         uint8_t *code = w.bel + o * NP;
         int a_bel = code[x.A];
         int d_bel = x.D >= 0 ? code[x.D] : BC_NONE;
-        if (x.fr_src) rem_dec(b, e, o, x.acting, SILING - 2);
-        if (x.fr_dst) rem_dec(b, e, o, x.D_seat, SILING - 2);
+        if (x.fr_src) inv |= rem_dec(w, o, x.acting, SILING - 2);
+        if (x.fr_dst) inv |= rem_dec(w, o, x.D_seat, SILING - 2);
         if (x.ev == EV_EAT && x.D >= 0 && x.D_type == DILEI && a_bel != BC_NONE && !bc_onehot(a_bel)) {
             code[x.A] = (uint8_t)(GONGB - 1);
             touched = true;
             a_bel = code[x.A];
-            rem_dec(b, e, o, x.acting, GONGB - 2);
+            inv |= rem_dec(w, o, x.acting, GONGB - 2);
         }
         if (x.fcap) {
-            if (x.D_seat >= 0 && x.D_seat < 4) rem_untrack(b, e, o, x.D_seat);
+            if (x.D_seat >= 0 && x.D_seat < 4) inv |= rem_untrack(w, o, x.D_seat);
         } else if (x.ev == EV_EAT && x.other_pid >= 0) {
             int op = x.other_pid;
             if (code[op] != BC_NONE && !bc_onehot(code[op])) {
@@ -661,17 +685,24 @@ __device__ void warp_belief_update(const jq_batch &b, const Topo &T, WEnv &w, in
         }
         a_bel = code[x.A];
         if (x.ev == EV_EAT) {
-            if (bc_onehot(d_bel)) rem_dec(b, e, o, x.D_seat, d_bel - 1);
+            if (bc_onehot(d_bel)) inv |= rem_dec(w, o, x.D_seat, d_bel - 1);
         } else if (x.ev == EV_KILLED) {
-            if (bc_onehot(a_bel)) rem_dec(b, e, o, x.acting, a_bel - 1);
+            if (bc_onehot(a_bel)) inv |= rem_dec(w, o, x.acting, a_bel - 1);
         } else if (x.ev == EV_BOMB) {
-            if (bc_onehot(a_bel)) rem_dec(b, e, o, x.acting, a_bel - 1);
-            if (bc_onehot(d_bel)) rem_dec(b, e, o, x.D_seat, d_bel - 1);
+            if (bc_onehot(a_bel)) inv |= rem_dec(w, o, x.acting, a_bel - 1);
+            if (bc_onehot(d_bel)) inv |= rem_dec(w, o, x.D_seat, d_bel - 1);
         }
         for (int s = 0; s < 4; ++s)
-            if (died[s]) rem_untrack(b, e, o, s);
+            if (died[s]) inv |= rem_untrack(w, o, s);
     }
     const bool any_touched = __any_sync(FULL, touched);
+    if (__any_sync(FULL, inv)) {  // write the inventories back in one pass
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < 4 * 4 * 12 / 32; ++i)
+            b.remaining[(size_t)e * 192 + lane + 32 * i] = w.rem[lane + 32 * i];
+        if (lane < 16) b.rem_tracked[(size_t)e * 16 + lane] = w.rtr[lane];
+    }
     // alive bits of pids 0..119 (bit p of word p >> 5)
     uint32_t am[4];
 #pragma unroll

@@ -47,13 +47,21 @@ def obs_timeline(t: np.ndarray) -> dict:
 
 
 def rules_timeline(t: np.ndarray) -> dict:
+    """Rules-kernel CTA exits, and the phases of each CTA's warp-0 env (us,
+    median / p90 / max over CTAs)."""
     t = t.astype(np.int64)
     t0 = t[:, 0].min()
     us = lambda a: (a - t0) / 1e3  # noqa: E731
-    return {"ctas": int(len(t)), "span_us": float(us(t[:, 2]).max()),
-            "waited_us_median": float(np.median(us(t[:, 1]))),
-            "exit_us_min": float(us(t[:, 2]).min()), "exit_us_median": float(np.median(us(t[:, 2]))),
-            "exit_us_p90": float(np.percentile(us(t[:, 2]), 90)), "exit_us_max": float(us(t[:, 2]).max())}
+    out = {"ctas": int(len(t)), "span_us": float(us(t[:, 7]).max()),
+           "waited_us_median": float(np.median(us(t[:, 1]))),
+           "exit_us_min": float(us(t[:, 7]).min()), "exit_us_median": float(np.median(us(t[:, 7]))),
+           "exit_us_p90": float(np.percentile(us(t[:, 7]), 90)), "exit_us_max": float(us(t[:, 7]).max())}
+    for name, a, b in (("load", 1, 2), ("step", 2, 3), ("reset", 3, 4), ("legal_ids", 4, 5), ("mask", 5, 6),
+                       ("env_total", 1, 6)):
+        d = (t[:, b] - t[:, a]) / 1e3
+        out[name + "_us"] = [round(float(np.median(d)), 2), round(float(np.percentile(d, 90)), 2),
+                             round(float(d.max()), 2)]
+    return out
 
 
 def main() -> None:
