@@ -497,9 +497,13 @@ def main() -> None:
         one_ply(t, [torch.cuda.Event(enable_timing=True) for _ in range(4)] if t % EVENT_EVERY == 0 else None)
     t0_ply = t + 1
     env.stats.zero_()  # jq_ply counts plies applied and episode statistics on the device
-    # Per-kernel CUDA events on every EVENT_EVERY-th timed ply: an event between
-    # two kernels keeps the next launch from overlapping the previous one's tail.
-    evs = {k: [torch.cuda.Event(enable_timing=True) for _ in range(4)] for k in range(0, args.steps, EVENT_EVERY)}
+    # Per-kernel CUDA events on every EVENT_EVERY-th timed ply (an event between
+    # two kernels keeps the next launch from overlapping the previous one's
+    # tail), from the 4th on: the first timed plies follow the synchronize
+    # above, so their events would also time the host submitting the kernels
+    # to an idle GPU.
+    evs = {k: [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+           for k in range(min(EVENT_EVERY // 2, args.steps - 1), args.steps, EVENT_EVERY)}
     start, end, ar0 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
     torch.cuda.synchronize()
     if world > 1:
@@ -568,8 +572,8 @@ def main() -> None:
             "pipeline": pipeline_roofline(value / world, seats, k_avg, peak),
             "clocks": summarize_clocks(clock_rows),
             "gpu_launches": 3 * args.steps,  # obs_kernel + sample kernel + rules_kernel per ply
-            "kernel_timing": f"CUDA events around each kernel on every {EVENT_EVERY}th timed ply "
-                             f"({len(obs_ms)} plies)",
+            "kernel_timing": f"CUDA events around each kernel on every {EVENT_EVERY}th timed ply from the "
+                             f"{min(EVENT_EVERY // 2, args.steps - 1)}th ({len(obs_ms)} plies)",
             "episode_stats": {"wins_team0": stats[0], "wins_team1": stats[1], "draws": stats[2],
                               "episodes": stats[3], "sum_len": stats[4]},
             "per_rank": per_rank,
