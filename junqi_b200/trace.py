@@ -1,13 +1,18 @@
 """Per-CTA timelines of the observation and rules kernels (tracing build).
 
     python -m junqi_b200.trace [--envs 4096] [--plies 200]
+    python -m junqi_b200.trace --sweep
 
 builds libjq_trace.so (the library compiled with JQ_TRACE: one %globaltimer
 store per CTA at a few points of each kernel, jq_trace.cuh), plays a
 configs[1]-style rollout (acting-seat observation, uniform policy, GameState
 rules) and prints, for the last ply's observation and rules launches, where
 their time goes: CTA start spread, wait for the previous kernel, the first
-unit's staging before any store, the streaming span and the tail.
+unit's staging before any store, the streaming span and the tail.  With
+--sweep it times instead (CUDA events, plain libjq.so) one observation and
+one ply launch at 1,024 ... 32,768 envs after a 200-ply burn-in, the median
+of 20 launches each, so the fixed and per-unit parts of each kernel's time
+can be separated.
 """
 from __future__ import annotations
 
@@ -64,11 +69,44 @@ def rules_timeline(t: np.ndarray) -> dict:
     return out
 
 
+def sweep() -> None:
+    import torch
+
+    from . import tables
+    from .env import JunqiEnvB200
+    N.build()
+    pool = tables.build_setup_pool(10_000, seed=42)
+    for n in (1024, 2048, 4096, 8192, 16384, 32768):
+        env = JunqiEnvB200(n, pool=pool, rules=N.RULES_GAMESTATE)
+        env.reset(seed=5)
+        for t in range(1, 201):
+            env.ply(env.sample_uniform(5, t), seed=5, ply=t)
+        s = torch.cuda.current_stream()
+        res = {}
+        for what in ("obs", "ply"):
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(42)]
+            for i in range(21):
+                a = env.sample_uniform(5, 300 + i) if what == "ply" else None
+                ev[2 * i].record(s)
+                env.observe() if what == "obs" else env.ply(a, seed=5, ply=300 + i)
+                ev[2 * i + 1].record(s)
+            torch.cuda.synchronize()
+            res[what] = sorted(ev[2 * i].elapsed_time(ev[2 * i + 1]) for i in range(1, 21))[10]
+        print(json.dumps({"envs": n, "obs_ms": round(res["obs"], 4), "ply_ms": round(res["ply"], 4),
+                          "obs_GBps": round(n * 376_480 / (res["obs"] / 1e3) / 1e9, 1)}), flush=True)
+        del env
+        torch.cuda.empty_cache()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--envs", type=int, default=4096)
     ap.add_argument("--plies", type=int, default=200)
+    ap.add_argument("--sweep", action="store_true", help="time both kernels over a range of batch sizes")
     args = ap.parse_args()
+    if args.sweep:
+        sweep()
+        return
     N.build(trace=True)
     N.use_trace_library()
     import torch
@@ -83,14 +121,12 @@ def main() -> None:
     torch.cuda.synchronize()
     env.observe()
     torch.cuda.synchronize()
-    st = N.lib()
     dev = torch.cuda.current_device()
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
     obs_ctas = min(2 * sms, args.envs)
     rule_ctas = min((args.envs + 7) // 8, 1024)
     print(json.dumps({"kernel": "obs_kernel", "units": args.envs, **obs_timeline(read(OBS, obs_ctas))}))
     print(json.dumps({"kernel": "rules_kernel", "envs": args.envs, **rules_timeline(read(RULES, rule_ctas))}))
-    del st
 
 
 if __name__ == "__main__":
