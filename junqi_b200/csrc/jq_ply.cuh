@@ -63,7 +63,7 @@ __device__ bool warp_ply_env(const RuleArgs &a, const Topo &T, WEnv &w, int e, i
         if (lane == 0) b.hist_count[e] = 0;
         __syncwarp();
     }
-    if (a.flags & DO_STEP) applied = warp_step(b, T, w, e, lane, a.acts[e], a.mode, a.out, a.stats);
+    if (a.flags & DO_STEP) applied = warp_step(b, T, w, e, lane, a.acts[e], a.mode, a.out, a.stats, traced);
     if (traced) JQ_TRACE_AT(1, TR_STEPPED);
     if ((a.flags & DO_RESET) && a.pool && a.pool_size > 0) {
         int row = -1;

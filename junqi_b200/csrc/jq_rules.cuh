@@ -15,8 +15,10 @@
 // parts -- the Q12 "has any legal move" checks, seat surrenders, the belief
 // sweep, resets and legal-move generation, where each of lanes 0..29 owns one
 // piece of the acting seat and computes its destination set as a 129-bit
-// mask over the compact board (engineer rail flood-fill as a frontier
-// expansion over per-cell rail-neighbour masks).
+// mask over the compact board (an engineer's rail run as a frontier
+// expansion over per-cell rail-neighbour masks in its own lane; the
+// path-revealed-engineer check of a move, which has one walk to do, as the
+// same expansion by the whole warp).
 #pragma once
 #include "jq_common.cuh"
 #include "jq_trace.cuh"
@@ -51,9 +53,11 @@ __device__ __forceinline__ int64_t zpiece(int pid, int t, int f) {
 // Per-warp shared-memory image of one env
 // ---------------------------------------------------------------------------
 struct StepCtx {
+    int64_t z_tail;  // Zobrist keys of the post-ply move counter and no-combat counter
     int skip, ev, A, D, sf, df, acting, A_type, A_seat, D_type, D_seat;
     int mc, mslc, new_mc, new_mslc, fcap, fr_src, fr_dst, other_pid, term, win, draw;
     int new_turn, need_surrender, do_q12, combat, full_advance;
+    int inv_async;  // the inventories are being copied into shared memory (cp.async)
     int cm;  // combat-memory update after the scalar part: 0 none, 1 EAT, 2 KILLED
     int died_pre[4];
 };
@@ -65,8 +69,8 @@ constexpr int CBW = (MASK_BYTES + 31) / 32 + 1;
 struct __align__(16) WEnv {
     uint32_t cbits[CBW];     // the canonical mask as one row-major bitstream (bit j = mask byte j)
     alignas(16) uint8_t bel[4 * NP];  // belief codes (observer-major), loaded with the state for a step
-    int16_t rem[4 * 4 * 12];  // enemy inventories (observer, seat, type), loaded when a ply changes them
-    uint8_t rtr[16];          // their tracked flags (observer, seat)
+    alignas(16) int16_t rem[4 * 4 * 12];  // enemy inventories (observer, seat, type), loaded when a ply changes them
+    alignas(16) uint8_t rtr[16];          // their tracked flags (observer, seat)
     uint64_t cmv[4][4];      // V's combat-memory sets per observer: direct lo/hi, chain lo/hi
     int32_t scan[32];
     StepCtx x;
@@ -82,6 +86,13 @@ struct __align__(16) WEnv {
     int8_t s_turn, s_term, s_win, s_draw;
     uint8_t sflag[4];  // seat_flag, kept in step with the global copy during the ply
 };
+
+// 16-byte global -> shared copy that does not pass through registers
+// (cp.async.cg: L2 only); both addresses 16-byte aligned.
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem) : "memory");
+}
 
 __device__ __forceinline__ size_t PI(int e, int p) { return (size_t)e * NP + p; }
 __device__ __forceinline__ size_t OI(int e, int o, int p) { return ((size_t)e * 4 + o) * NP + p; }
@@ -177,7 +188,8 @@ __device__ void piece_dsts(const Topo &T, int c, int t, const uint32_t (&empty)[
     }
     if (!(T.flags[c] & F_RAIL)) return;
     if (t == GONGB) {
-        // engineer: cells adjacent to the set reached through empty rail cells
+        // engineer: cells adjacent to the set reached through empty rail
+        // cells, one lane per engineer (the side's engineers expand at once)
         uint32_t reach[NW], fr[NW], landing[NW];
 #pragma unroll
         for (int i = 0; i < NW; ++i) reach[i] = fr[i] = landing[i] = 0;
@@ -272,7 +284,7 @@ __device__ __forceinline__ int lane_source(const WEnv &w, int lane, int seat) {
 
 // has_legal_moves_soa (move_gen.py:1557-1609): any legal action for `seat`,
 // ignoring terminated / dead flags.
-__device__ bool warp_has_moves(const Topo &T, const WEnv &w, int lane, int seat) {
+__device__ bool warp_has_moves(const Topo &T, const WEnv &w, int lane, int seat, int *full_scans = nullptr) {
     uint32_t empty[NW], land[NW], d[NW];
     board_masks(T, w, lane, seat & 1, empty, land);
     int src = lane_source(w, lane, seat);
@@ -290,6 +302,7 @@ __device__ bool warp_has_moves(const Topo &T, const WEnv &w, int lane, int seat)
             }
     }
     if (__any_sync(FULL, quick)) return true;
+    if (full_scans) ++*full_scans;
     bool any = false;
     if (src >= 0) {
         piece_dsts(T, src, w.type[seat * 30 + lane], empty, land, d);
@@ -402,41 +415,49 @@ __device__ bool ray_clear_to(const Topo &T, const WEnv &w, const uint8_t *ray, i
     return false;
 }
 
-__device__ bool engineer_reach(const Topo &T, const WEnv &w, int s, int d) {
+// Whether an engineer on compact cell s reaches d along the railway through
+// empty cells (move_gen.py:186-224), by the whole warp (the result on every
+// lane): lane l tests cells l, l + 32, ... for a rail neighbour in the
+// frontier (the rail graph is symmetric), and one ballot per mask word
+// gathers the next frontier, so an expansion costs a few shared loads per
+// lane instead of one lane's serial walk over the frontier's neighbours.
+__device__ bool warp_engineer_reach(const Topo &T, const WEnv &w, int lane, int s, int d) {
     if (!(T.flags[s] & F_RAIL) || !(T.flags[d] & F_RAIL) || s == d) return false;
-    uint32_t reach[NW] = {0, 0, 0, 0, 0}, fr[NW] = {0, 0, 0, 0, 0};
+    uint32_t empty[NW], reach[NW] = {0, 0, 0, 0, 0}, fr[NW] = {0, 0, 0, 0, 0};
+#pragma unroll
+    for (int i = 0; i < NW; ++i) {
+        const int c = i * 32 + lane;
+        empty[i] = __ballot_sync(FULL, c < NB && w.cell[T.c2f[c]] < 0);
+    }
     rset(reach, s);
     rset(fr, s);
     for (int it = 0; it < NB; ++it) {
-        uint32_t nbm[NW] = {0, 0, 0, 0, 0};
-        for (int wd = 0; wd < NW; ++wd) {
-            uint32_t m = fr[wd];
-            while (m) {
-                int v = wd * 32 + __ffs(m) - 1;
-                m &= m - 1;
-                for (int i = 0; i < NW; ++i) nbm[i] |= T.railnb[v][i];
-            }
+        uint32_t nbm[NW];
+#pragma unroll
+        for (int i = 0; i < NW; ++i) {
+            const int c = i * 32 + lane;
+            bool hit = false;
+            if (c < NB)
+#pragma unroll
+                for (int k = 0; k < NW; ++k)
+                    if (fr[k]) hit |= (T.railnb[c][k] & fr[k]) != 0u;  // fr is the same on every lane
+            nbm[i] = __ballot_sync(FULL, hit);
         }
         if (rbit(nbm, d)) return true;
         uint32_t any = 0;
+#pragma unroll
         for (int i = 0; i < NW; ++i) {
-            uint32_t nw = nbm[i] & ~reach[i];
-            uint32_t keep = 0, mm = nw;
-            while (mm) {
-                int v = i * 32 + __ffs(mm) - 1;
-                mm &= mm - 1;
-                if (w.cell[T.c2f[v]] < 0) keep |= 1u << (v & 31);
-            }
-            reach[i] |= keep;
-            fr[i] = keep;
-            any |= keep;
+            const uint32_t nw = nbm[i] & empty[i] & ~reach[i];
+            reach[i] |= nw;
+            fr[i] = nw;
+            any |= nw;
         }
         if (!any) break;
     }
     return false;
 }
 
-__device__ bool move_requires_gongb(const Topo &T, const WEnv &w, int sf, int df) {
+__device__ bool move_requires_gongb(const Topo &T, const WEnv &w, int sf, int df, int lane) {
     if (sf == df) return false;
     int sx = sf % 17, sy = sf / 17, dx = df % 17, dy = df / 17;
     int adx = abs(sx - dx), ady = abs(sy - dy);
@@ -448,13 +469,13 @@ __device__ bool move_requires_gongb(const Topo &T, const WEnv &w, int sf, int df
     if (sx == dx || sy == dy) {
         for (int k = 0; k < 4; ++k)
             if (ray_clear_to(T, w, T.sray[s][k], 12, d)) return false;
-        return engineer_reach(T, w, s, d);
+        return warp_engineer_reach(T, w, lane, s, d);
     }
     if (T.curve[s] > 0 && T.curve[s] == T.curve[d] && (T.flags[s] & F_CURVE_ACTIVE)) {
         for (int k = 0; k < 2; ++k)
             if (ray_clear_to(T, w, T.cray[s][k], 11, d)) return false;
     }
-    return engineer_reach(T, w, s, d);
+    return warp_engineer_reach(T, w, lane, s, d);
 }
 
 // ---------------------------------------------------------------------------
@@ -484,13 +505,25 @@ __device__ void warp_cm_apply(const jq_batch &b, WEnv &w, int e, int lane, bool 
                               int D_seat, int A_type, int D_type, int step) {
     const int K = eat ? A : D, V = eat ? D : A, V_seat = eat ? D_seat : A_seat, V_type = eat ? D_type : A_type;
     const int v_idx = tracked_idx(V_type);
+    // One round of loads: V's sets (lanes 0..15, one word each), K's rows
+    // (lanes 0..3) and the eaten-by rows of pid o * 30 + lane for every
+    // observer o (lanes 0..29), the last before knowing which of them gain K.
+    uint64_t vset = 0;
     if (lane < 16) {
         const int o = lane >> 2, f = lane & 3;
         const uint64_t *src = f == 0 ? b.cm_direct_lo : f == 1 ? b.cm_direct_hi : f == 2 ? b.cm_chain_lo : b.cm_chain_hi;
-        w.cmv[o][f] = src[OI(e, o, V)];
+        vset = src[OI(e, o, V)];
     }
-    __syncwarp();
-    // loads: K's row of observer o = lane (lanes 0..3) ...
+    uint64_t ea[4], eb[4];
+#pragma unroll
+    for (int o = 0; o < 4; ++o) {
+        ea[o] = eb[o] = 0;
+        if (lane < 30) {
+            ea[o] = b.cm_eaten_lo[OI(e, o, o * 30 + lane)];
+            eb[o] = b.cm_eaten_hi[OI(e, o, o * 30 + lane)];
+        }
+    }
+    // K's row of observer o = lane (lanes 0..3)
     const int o4 = lane & 3;
     const size_t k = OI(e, o4, K), v = OI(e, o4, V);
     uint8_t g_v = 0;
@@ -511,20 +544,16 @@ __device__ void warp_cm_apply(const jq_batch &b, WEnv &w, int e, int lane, bool 
         dk_hi = b.cm_direct_hi[k];
         dk_t = b.cm_direct_type[k];
     }
-    // ... and the eaten-by rows of pid o * 30 + lane that gain K: those in V's
-    // direct or chain set of observer o, or V itself
+    if (lane < 16) w.cmv[lane >> 2][lane & 3] = vset;
+    __syncwarp();
+    // the eaten-by rows that gain K: pids in V's direct or chain set of
+    // observer o, or V itself
     bool on[4];
-    uint64_t ea[4], eb[4];
 #pragma unroll
     for (int o = 0; o < 4; ++o) {
         const int t = o * 30 + lane;
         const uint64_t lo = w.cmv[o][0] | w.cmv[o][2], hi = w.cmv[o][1] | w.cmv[o][3];
         on[o] = lane < 30 && ((t < 64 ? (lo >> t) & 1ull : (hi >> (t - 64)) & 1ull) || (V_seat == o && t == V));
-        ea[o] = eb[o] = 0;
-        if (on[o]) {
-            ea[o] = b.cm_eaten_lo[OI(e, o, t)];
-            eb[o] = b.cm_eaten_hi[OI(e, o, t)];
-        }
     }
     if (lane < 4) {
         const int o = lane;
@@ -652,10 +681,14 @@ __device__ void warp_belief_update(const jq_batch &b, const Topo &T, WEnv &w, in
     bool touched = false;  // R-rules rewrote a code of this lane's observer
     bool inv = false;      // ... or an inventory entry
     // Only combat plies and seat deaths change inventories: then the env's
-    // 192 entries and 16 tracked flags come into shared memory in one round
-    // trip, the rules run there, and the rows are written back once.
-    const bool inv_ply = x.combat || died[0] || died[1] || died[2] || died[3];
-    if (inv_ply) {
+    // 192 entries and 16 tracked flags are in shared memory (a combat ply
+    // started copying them before its combat-memory update; otherwise they
+    // are loaded here in one round trip), the rules run there, and the rows
+    // are written back once.
+    if (x.inv_async) {
+        asm volatile("cp.async.wait_all;" ::: "memory");
+        __syncwarp();
+    } else if (x.combat || died[0] || died[1] || died[2] || died[3]) {
 #pragma unroll
         for (int i = 0; i < 4 * 4 * 12 / 32; ++i) w.rem[lane + 32 * i] = b.remaining[(size_t)e * 192 + lane + 32 * i];
         if (lane < 16) w.rtr[lane] = b.rem_tracked[(size_t)e * 16 + lane];
@@ -909,7 +942,7 @@ __device__ __forceinline__ void move_piece(const jq_batch &b, const Topo &T, WEn
 
 // Returns true on every lane when the ply was applied.
 __device__ bool warp_step(const jq_batch &b, const Topo &T, WEnv &w, int e, int lane, int32_t act, int mode,
-                          const jq_step_out &out, int64_t *stats) {
+                          const jq_step_out &out, int64_t *stats, bool traced = false) {
     StepCtx &x = w.x;
     int64_t zob = 0;
     if (lane == 0) {
@@ -937,6 +970,13 @@ __device__ bool warp_step(const jq_batch &b, const Topo &T, WEnv &w, int e, int 
     }
     __syncwarp();
     if (x.skip) return false;
+    // path-revealed engineer (move_gen.py:245-296) on the pre-move board, by
+    // the whole warp: a move only an engineer's rail run can make
+    bool gongb_path = false;
+    if (x.A_type == GONGB) {
+        const int adx = abs(x.sf % 17 - x.df % 17), ady = abs(x.sf / 17 - x.df / 17);
+        if (x.D >= 0 || adx + ady > 1) gongb_path = move_requires_gongb(T, w, x.sf, x.df, lane);
+    }
     if (lane == 0) {
         const int sf = x.sf, df = x.df, A = x.A, D = x.D;
         x.acting = w.s_turn;
@@ -954,16 +994,25 @@ __device__ bool warp_step(const jq_batch &b, const Topo &T, WEnv &w, int e, int 
             if (df == s0) x.other_pid = w.cell[s1];
             else if (df == s1) x.other_pid = w.cell[s0];
         }
-        if (x.A_type == GONGB) {
-            int adx = abs(sf % 17 - df % 17), ady = abs(sf / 17 - df / 17);
-            if ((D >= 0 || adx + ady > 1) && move_requires_gongb(T, w, sf, df))
-                for (int o = 0; o < 4; ++o) b.cm_is_gongb[OI(e, o, A)] = 1;
-        }
-        zob = w.s_zob ^ c_zturn[x.acting & 3] ^ g_zmc[x.mc & 0xFFF] ^ g_zmslc[x.mslc & 0x1FF];
+        // Every global value the ply reads, loaded before its first global
+        // store: the compiler cannot move a load past a store that may alias
+        // it, so loads issued where they are used would each wait a full
+        // round trip behind the stores before them.
+        const int64_t zA_src = zpiece(A, x.A_type, sf), zA_dst = zpiece(A, x.A_type, df);
+        const int64_t zD_dst = D >= 0 ? zpiece(D, x.D_type, df) : 0;
+        const int64_t z_mc = g_zmc[x.mc & 0xFFF], z_mslc = g_zmslc[x.mslc & 0x1FF];
+        const int64_t z_mc1 = g_zmc[(x.mc + 1) & 0xFFF], z_mslc1 = g_zmslc[D < 0 ? (x.mslc + 1) & 0x1FF : 0];
+        const int cnt = D < 0 ? b.move_count[PI(e, A)]
+                        : x.ev == EV_EAT ? b.active_eat[PI(e, A)]
+                        : x.ev == EV_KILLED ? b.passive_surv[PI(e, D)] : 0;
+        if (gongb_path)
+            for (int o = 0; o < 4; ++o) b.cm_is_gongb[OI(e, o, A)] = 1;
+        zob = w.s_zob ^ c_zturn[x.acting & 3] ^ z_mc ^ z_mslc;
+        x.z_tail = z_mc1 ^ z_mslc1;
         if (D < 0) {
-            zob ^= zpiece(A, x.A_type, sf) ^ zpiece(A, x.A_type, df);
+            zob ^= zA_src ^ zA_dst;
             move_piece(b, T, w, e, A, sf, df);
-            b.move_count[PI(e, A)]++;
+            b.move_count[PI(e, A)] = (int16_t)(cnt + 1);
             x.new_mslc = x.mslc + 1;
         } else {
             int ds = x.new_mc;
@@ -981,20 +1030,20 @@ __device__ bool warp_step(const jq_batch &b, const Topo &T, WEnv &w, int e, int 
             }
             x.fcap = x.D_type == JUNQI;
             if (x.ev == EV_EAT) {
-                zob ^= zpiece(D, x.D_type, df);
+                zob ^= zD_dst;
                 kill_piece(b, T, w, e, D, df, DR_KBE, ds, df);
-                zob ^= zpiece(A, x.A_type, sf) ^ zpiece(A, x.A_type, df);
+                zob ^= zA_src ^ zA_dst;
                 move_piece(b, T, w, e, A, sf, df);
-                b.active_eat[PI(e, A)]++;
+                b.active_eat[PI(e, A)] = (int16_t)(cnt + 1);
                 x.cm = 1;
             } else if (x.ev == EV_KILLED) {
                 int dr = (x.D_type == DILEI || x.D_type == ZHADAN) ? DR_MINE : DR_KBE;
-                zob ^= zpiece(A, x.A_type, sf);
+                zob ^= zA_src;
                 kill_piece(b, T, w, e, A, sf, dr, ds, df);
-                b.passive_surv[PI(e, D)]++;
+                b.passive_surv[PI(e, D)] = (int16_t)(cnt + 1);
                 x.cm = 2;
             } else {
-                zob ^= zpiece(A, x.A_type, sf) ^ zpiece(D, x.D_type, df);
+                zob ^= zA_src ^ zD_dst;
                 kill_piece(b, T, w, e, A, sf, DR_MUTUAL, ds, df);
                 kill_piece(b, T, w, e, D, df, DR_MUTUAL, ds, df);
             }
@@ -1010,6 +1059,19 @@ __device__ bool warp_step(const jq_batch &b, const Topo &T, WEnv &w, int e, int 
         }
     }
     __syncwarp();
+    if (traced) {
+        JQ_TRACE_AT(1, TR_SCALAR);
+        JQ_TRACE_COUNT(1, TR_EVENT, x.ev);
+    }
+    // A combat ply changes inventories: they are copied into shared memory
+    // asynchronously (cp.async, no registers held) while the combat-memory
+    // update runs, and the belief update waits for the copy.
+    x.inv_async = x.combat && !(((uintptr_t)b.remaining | (uintptr_t)b.rem_tracked) & 15);
+    if (x.inv_async) {
+        if (lane < 24) cp_async16(&w.rem[lane * 8], b.remaining + (size_t)e * 192 + lane * 8);
+        else if (lane == 24) cp_async16(w.rtr, b.rem_tracked + (size_t)e * 16);
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    }
     if (x.cm) warp_cm_apply(b, w, e, lane, x.cm == 1, x.A, x.D, x.A_seat, x.D_seat, x.A_type, x.D_type, x.new_mc);
     if (x.need_surrender) {
         int64_t d = warp_surrender(b, T, w, e, lane, x.D_seat, x.new_mc);
@@ -1043,12 +1105,14 @@ __device__ bool warp_step(const jq_batch &b, const Topo &T, WEnv &w, int e, int 
         x.new_turn = x.full_advance ? (x.term ? x.acting : (x.acting + 1) & 3) : cand;
     }
     __syncwarp();
+    if (traced) JQ_TRACE_AT(1, TR_COMBAT);
+    int scans = 0;
     if (x.do_q12) {
         int cand = (x.acting + 1) & 3, chain = 0;
         bool found = false;
         while (chain < 4) {
             if (w.sdead[cand]) { cand = (cand + 1) & 3; ++chain; continue; }
-            if (warp_has_moves(T, w, lane, cand)) { found = true; break; }
+            if (warp_has_moves(T, w, lane, cand, &scans)) { found = true; break; }
             int64_t d = warp_surrender(b, T, w, e, lane, cand, x.new_mc);
             if (lane == 0) zob ^= d;
             cand = (cand + 1) & 3;
@@ -1060,13 +1124,17 @@ __device__ bool warp_step(const jq_batch &b, const Topo &T, WEnv &w, int e, int 
         }
     }
     __syncwarp();
+    if (traced) {
+        JQ_TRACE_AT(1, TR_Q12);
+        JQ_TRACE_COUNT(1, TR_Q12_SCANS, scans);
+    }
     if (lane == 0) {
         // the caller's episode cap, after victory and Q12 (game_state.cu:1651-1655)
         if (!x.term && b.max_moves > 0 && x.new_mc >= b.max_moves) {
             x.term = 1;
             x.draw = 1;
         }
-        zob ^= g_zmc[x.new_mc & 0xFFF] ^ g_zmslc[x.new_mslc & 0x1FF] ^ c_zturn[x.new_turn & 3];
+        zob ^= x.z_tail ^ c_zturn[x.new_turn & 3];  // keys of new_mc and new_mslc
         if (x.term) zob ^= c_zterm;
         if (x.draw) zob ^= c_zdraw;
         if (x.win >= 0) zob ^= c_zwin[0] ^ c_zwin[x.win + 1];
@@ -1098,6 +1166,7 @@ __device__ bool warp_step(const jq_batch &b, const Topo &T, WEnv &w, int e, int 
         }
     }
     __syncwarp();
+    if (traced) JQ_TRACE_AT(1, TR_COMMIT);
     int died[4];
 #pragma unroll
     for (int s = 0; s < 4; ++s) died[s] = w.sdead[s] && !x.died_pre[s];

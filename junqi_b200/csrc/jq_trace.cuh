@@ -14,14 +14,18 @@ namespace jq {
 
 constexpr int TRACE_KERNELS = 2;   // 0: obs_kernel, 1: rules_kernel
 constexpr int TRACE_CTAS = 1024;   // CTAs recorded per launch (grid beyond this is not traced)
-constexpr int TRACE_POINTS = 8;
+constexpr int TRACE_POINTS = 16;
 
 // obs_kernel points
 enum : int { TO_ENTRY = 0, TO_WAITED = 1, TO_FIRST_STAGED = 2, TO_FIRST_STREAM = 3, TO_LAST_STREAMED = 4,
              TO_EXIT = 5, TO_UNITS = 6 };
 // rules_kernel points (the phases of warp 0's first env, then the CTA's exit)
 enum : int { TR_ENTRY = 0, TR_WAITED = 1, TR_LOADED = 2, TR_STEPPED = 3, TR_RESET = 4, TR_IDS = 5, TR_MASKED = 6,
-             TR_EXIT = 7 };
+             TR_EXIT = 7,
+             // inside the step of the same env
+             TR_SCALAR = 8, TR_COMBAT = 9, TR_Q12 = 10, TR_COMMIT = 11,
+             // counts: the env's event (0: no step), Q12 full destination scans
+             TR_EVENT = 12, TR_Q12_SCANS = 13 };
 
 #ifdef JQ_TRACE
 __device__ uint64_t g_trace[TRACE_KERNELS][TRACE_CTAS][TRACE_POINTS];

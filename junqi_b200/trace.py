@@ -26,9 +26,12 @@ from . import _native as N
 OBS, RULES = 0, 1
 
 
+POINTS = 16
+
+
 def read(kernel: int, ctas: int) -> np.ndarray:
-    """(ctas, 8) uint64 timestamps of the last launch of `kernel`."""
-    out = np.zeros((ctas, 8), np.uint64)
+    """(ctas, POINTS) uint64 timestamps (and counts) of the last launch of `kernel`."""
+    out = np.zeros((ctas, POINTS), np.uint64)
     N.check(N.lib().jq_trace_read(kernel, out.ctypes.data, ctas), "jq_trace_read")
     return out
 
@@ -61,11 +64,20 @@ def rules_timeline(t: np.ndarray) -> dict:
            "waited_us_median": float(np.median(us(t[:, 1]))),
            "exit_us_min": float(us(t[:, 7]).min()), "exit_us_median": float(np.median(us(t[:, 7]))),
            "exit_us_p90": float(np.percentile(us(t[:, 7]), 90)), "exit_us_max": float(us(t[:, 7]).max())}
-    for name, a, b in (("load", 1, 2), ("step", 2, 3), ("reset", 3, 4), ("legal_ids", 4, 5), ("mask", 5, 6),
-                       ("env_total", 1, 6)):
+    for name, a, b in (("load", 1, 2), ("step", 2, 3), ("step_scalar", 2, 8), ("step_combat", 8, 9),
+                       ("step_q12", 9, 10), ("step_commit", 10, 11), ("step_beliefs", 11, 3), ("reset", 3, 4),
+                       ("legal_ids", 4, 5), ("mask", 5, 6), ("env_total", 1, 6)):
         d = (t[:, b] - t[:, a]) / 1e3
         out[name + "_us"] = [round(float(np.median(d)), 2), round(float(np.percentile(d, 90)), 2),
                              round(float(d.max()), 2)]
+    # the slowest envs: their phases, event and Q12 full scans
+    slow = np.argsort((t[:, 6] - t[:, 1]))[-5:]
+    out["slowest"] = [{"total": round((t[i, 6] - t[i, 1]) / 1e3, 1), "load": round((t[i, 2] - t[i, 1]) / 1e3, 1),
+                       "scalar": round((t[i, 8] - t[i, 2]) / 1e3, 1), "combat": round((t[i, 9] - t[i, 8]) / 1e3, 1),
+                       "q12": round((t[i, 10] - t[i, 9]) / 1e3, 1), "commit": round((t[i, 11] - t[i, 10]) / 1e3, 1),
+                       "beliefs": round((t[i, 3] - t[i, 11]) / 1e3, 1), "ids": round((t[i, 5] - t[i, 4]) / 1e3, 1),
+                       "mask": round((t[i, 6] - t[i, 5]) / 1e3, 1), "event": int(t[i, 12]),
+                       "q12_scans": int(t[i, 13])} for i in slow]
     return out
 
 
