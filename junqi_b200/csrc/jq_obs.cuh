@@ -599,11 +599,13 @@ __global__ void __launch_bounds__(OBS_THREADS, OBS_MIN_CTAS) obs_kernel(jq_batch
             stage_unit(b, seats, mode, ext_bel, global, S, B, u, o, unit_head(spatial, u), t, BAR_STAGE);
             bar_sync(BAR_STAGE, OBS_STAGE_THREADS);    // unit staged by every staging thread
             if (k == 0 && t == 0) JQ_TRACE_AT(0, TO_FIRST_STAGED);
+            if (t == 0) JQ_TRACE_AT(0, TO_LAST_STAGED);
             bar_arrive(BAR_FULL0 + bi, OBS_THREADS);  // hand it to the streaming warps
             if (t == 0) {
                 const int un = atomicAdd(&ticket[0], 1);
                 S.ticket[0] = un;
                 S.next_o[0] = un < units ? unit_observer(b, observers, seats, un) : 0;
+                if (un < units) JQ_TRACE_AT(0, TO_LAST_TICKET);
             }
             bar_sync(BAR_STAGE, OBS_STAGE_THREADS);  // next ticket published
             u = S.ticket[0];

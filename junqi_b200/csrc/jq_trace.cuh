@@ -18,7 +18,7 @@ constexpr int TRACE_POINTS = 16;
 
 // obs_kernel points
 enum : int { TO_ENTRY = 0, TO_WAITED = 1, TO_FIRST_STAGED = 2, TO_FIRST_STREAM = 3, TO_LAST_STREAMED = 4,
-             TO_EXIT = 5, TO_UNITS = 6 };
+             TO_EXIT = 5, TO_UNITS = 6, TO_LAST_TICKET = 7, TO_LAST_STAGED = 8 };
 // rules_kernel points (the phases of warp 0's first env, then the CTA's exit)
 enum : int { TR_ENTRY = 0, TR_WAITED = 1, TR_LOADED = 2, TR_STEPPED = 3, TR_RESET = 4, TR_IDS = 5, TR_MASKED = 6,
              TR_EXIT = 7,

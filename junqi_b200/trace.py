@@ -51,7 +51,25 @@ def obs_timeline(t: np.ndarray) -> dict:
             "last_streamed_us_min": float(us(t[:, 4]).min()),
             "last_streamed_us_median": float(np.median(us(t[:, 4]))),
             "exit_us_min": float(us(t[:, 5]).min()), "exit_us_max": float(us(t[:, 5]).max()),
-            "units_per_cta_min": int(t[:, 6].min()), "units_per_cta_max": int(t[:, 6].max())}
+            "units_per_cta_min": int(t[:, 6].min()), "units_per_cta_max": int(t[:, 6].max()),
+            # the tail: exits after the last ticket was taken (T0), split by whether the CTA
+            # still had a staged unit waiting behind the one it was streaming at T0
+            "tail_after_last_ticket_us": _tail(t)}
+
+
+def _tail(t: np.ndarray) -> dict:
+    """Exits after T0, the moment the last unit's ticket was taken; for the
+    CTAs that exit last, when they took their own last ticket and finished
+    staging it, relative to T0 (us)."""
+    took = t[:, 7] > 0
+    t0 = t[took, 7].max() if took.any() else t[:, 5].min()
+    rel = lambda a: (a - t0) / 1e3  # noqa: E731
+    after = rel(t[:, 5])
+    last = np.argsort(after)[-6:]
+    return {"exit_after_t0_p10_p50_max": [round(float(np.percentile(after, 10)), 1),
+                                          round(float(np.median(after)), 1), round(float(after.max()), 1)],
+            "latest_exits": [{"exit": round(float(after[i]), 1), "last_ticket": round(float(rel(t[i, 7])), 1),
+                              "last_staged": round(float(rel(t[i, 8])), 1), "units": int(t[i, 6])} for i in last]}
 
 
 def rules_timeline(t: np.ndarray) -> dict:
