@@ -333,6 +333,7 @@ __device__ int warp_legal(const Topo &T, WEnv &w, int lane, int seat, bool skip,
     int src = skip ? -1 : lane_source(w, lane, seat);
     if (src >= 0) piece_dsts(T, src, w.type[seat * 30 + lane], empty, land, d);
     int cnt = __popc(d[0]) + __popc(d[1]) + __popc(d[2]) + __popc(d[3]) + __popc(d[4]);
+    if (traced) JQ_TRACE_AT(1, TR_DSTS);  // lane 0 only: no warp barrier here
     // rank of the source among all sources (compact order == flat order)
     int rank = 0;
 #pragma unroll
@@ -357,6 +358,7 @@ __device__ int warp_legal(const Topo &T, WEnv &w, int lane, int seat, bool skip,
     __syncwarp();
     w.scan[lane] = inc - v;
     __syncwarp();
+    if (traced) JQ_TRACE_AT(1, TR_RANKED);
     if (src >= 0 && ids) {
         int off = w.scan[rank];
         int base = T.c2f[src] * NC;

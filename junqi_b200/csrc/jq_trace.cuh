@@ -25,7 +25,9 @@ enum : int { TR_ENTRY = 0, TR_WAITED = 1, TR_LOADED = 2, TR_STEPPED = 3, TR_RESE
              // inside the step of the same env
              TR_SCALAR = 8, TR_COMBAT = 9, TR_Q12 = 10, TR_COMMIT = 11,
              // counts: the env's event (0: no step), Q12 full destination scans
-             TR_EVENT = 12, TR_Q12_SCANS = 13 };
+             TR_EVENT = 12, TR_Q12_SCANS = 13,
+             // inside legal generation: destination sets done, ranking and scan done
+             TR_DSTS = 14, TR_RANKED = 15 };
 
 #ifdef JQ_TRACE
 __device__ uint64_t g_trace[TRACE_KERNELS][TRACE_CTAS][TRACE_POINTS];

@@ -84,7 +84,8 @@ def rules_timeline(t: np.ndarray) -> dict:
            "exit_us_p90": float(np.percentile(us(t[:, 7]), 90)), "exit_us_max": float(us(t[:, 7]).max())}
     for name, a, b in (("load", 1, 2), ("step", 2, 3), ("step_scalar", 2, 8), ("step_combat", 8, 9),
                        ("step_q12", 9, 10), ("step_commit", 10, 11), ("step_beliefs", 11, 3), ("reset", 3, 4),
-                       ("legal_ids", 4, 5), ("mask", 5, 6), ("env_total", 1, 6)):
+                       ("legal_ids", 4, 5), ("legal_dsts", 4, 14), ("legal_rank", 14, 15), ("legal_store", 15, 5),
+                       ("mask", 5, 6), ("env_total", 1, 6)):
         d = (t[:, b] - t[:, a]) / 1e3
         out[name + "_us"] = [round(float(np.median(d)), 2), round(float(np.percentile(d, 90)), 2),
                              round(float(d.max()), 2)]
@@ -94,6 +95,7 @@ def rules_timeline(t: np.ndarray) -> dict:
                        "scalar": round((t[i, 8] - t[i, 2]) / 1e3, 1), "combat": round((t[i, 9] - t[i, 8]) / 1e3, 1),
                        "q12": round((t[i, 10] - t[i, 9]) / 1e3, 1), "commit": round((t[i, 11] - t[i, 10]) / 1e3, 1),
                        "beliefs": round((t[i, 3] - t[i, 11]) / 1e3, 1), "ids": round((t[i, 5] - t[i, 4]) / 1e3, 1),
+                       "dsts": round((t[i, 14] - t[i, 4]) / 1e3, 1), "rank": round((t[i, 15] - t[i, 14]) / 1e3, 1),
                        "mask": round((t[i, 6] - t[i, 5]) / 1e3, 1), "event": int(t[i, 12]),
                        "q12_scans": int(t[i, 13])} for i in slow]
     return out

@@ -122,3 +122,31 @@ def test_no_host_pointer_is_taken_from_a_temporary_array():
             if re.search(r"\)\s*\.ctypes\.data\b", line):
                 bad.append(f"{p.name}:{i}: {line.strip()}")
     assert not bad, "pointers taken from temporaries:\n" + "\n".join(bad)
+
+
+def test_trace_points_hold_no_warp_collectives():
+    """The rules kernel's trace points run on lane 0 of one warp only
+    (`traced`); a warp barrier, ballot or shuffle inside such a block would
+    wait for 31 lanes that never arrive and hang the kernel -- in the
+    normal build too, where only the stores are compiled out."""
+    import re
+    from pathlib import Path
+    csrc = Path(__file__).resolve().parent.parent / "junqi_b200" / "csrc"
+    collective = re.compile(r"__syncwarp|__ballot_sync|__shfl|__any_sync|__all_sync|__reduce_|bar_sync|bar_arrive|"
+                            r"__syncthreads")
+    bad = []
+    for p in sorted(csrc.glob("*.cu*")):
+        lines = p.read_text().splitlines()
+        for i, line in enumerate(lines):
+            if not re.search(r"\bif \(traced\)", line):
+                continue
+            body = [line]
+            if line.rstrip().endswith("{"):
+                depth, j = 1, i + 1
+                while depth and j < len(lines):
+                    depth += lines[j].count("{") - lines[j].count("}")
+                    body.append(lines[j])
+                    j += 1
+            if any(collective.search(b) for b in body):
+                bad.append(f"{p.name}:{i + 1}")
+    assert not bad, "warp collectives inside lane-0 trace blocks: " + ", ".join(bad)
