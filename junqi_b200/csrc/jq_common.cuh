@@ -51,7 +51,8 @@ struct __align__(16) Topo {
     uint8_t diag[NB][4];       // diagonal steps into / out of a camp
     uint8_t sray[NB][4][12];   // straight rail rays (+x,-x,+y,-y)
     uint8_t cray[NB][2][11];   // curve-chain rays (forward, backward)
-    uint32_t railnb[NB][NW];   // rail-graph neighbours as a mask
+    alignas(16) uint32_t railnb[NB][8];  // rail-graph neighbours as a mask; words NW.. are zero, so a
+                                         // row loads as two 16-byte words
     uint8_t rot[4][NB];        // world compact -> canonical compact, per seat
     int16_t rotf[4][NC];       // world flat -> canonical flat, per seat
     uint8_t slot_cell[4][30];  // compact cell of (seat, slot)

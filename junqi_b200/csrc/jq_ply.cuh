@@ -17,6 +17,9 @@ struct RuleSmem {
     int applied;  // plies applied by this CTA (statistics)
 };
 
+// four CTAs per SM (one wave at 4,096 envs): 228 KB of shared memory, 1 KB reserved per CTA
+static_assert(sizeof(RuleSmem) + 1024 <= 228 * 1024 / 4, "rules kernel shared memory exceeds four CTAs per SM");
+
 struct RuleArgs {
     jq_batch b;
     const int32_t *acts;

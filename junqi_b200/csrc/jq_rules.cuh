@@ -203,8 +203,13 @@ __device__ void piece_dsts(const Topo &T, int c, int t, const uint32_t (&empty)[
                 while (m) {
                     int v = wd * 32 + __ffs(m) - 1;
                     m &= m - 1;
-#pragma unroll
-                    for (int i = 0; i < NW; ++i) nbm[i] |= T.railnb[v][i];
+                    const uint4 *row = reinterpret_cast<const uint4 *>(T.railnb[v]);
+                    const uint4 r0 = row[0], r1 = row[1];
+                    nbm[0] |= r0.x;
+                    nbm[1] |= r0.y;
+                    nbm[2] |= r0.z;
+                    nbm[3] |= r0.w;
+                    nbm[4] |= r1.x;
                 }
             }
             uint32_t any = 0;
