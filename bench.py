@@ -220,7 +220,27 @@ def reference_arm(args, cfg: dict) -> None:
     print(json.dumps(line), flush=True)
 
 
-def _junqi_core_worker(rank: int, envs: int, burn_in: int, budget_s: float, seed: int, q) -> None:
+def _batched_worker(rank: int, envs: int, budget_s: float, seed: int, q) -> None:
+    """junqi_core's vectorised path on one core: BatchedGameState.step_batch
+    (batched_state.py:417) + legal_action_ids_batch (:370) over `envs` games,
+    a uniform legal action each; finished games stay finished."""
+    import random
+    sys.path.insert(0, str(ROOT / "baseline" / "_ref"))
+    from junqi_core.batched_state import BatchedGameState
+    from junqi_core.setup import generate_random_setup
+    from junqi_core.state import GameState
+    rng = random.Random(seed + 7919 * rank)
+    b = BatchedGameState.from_game_states(
+        [GameState.new_game(generate_random_setup(random.Random(rng.getrandbits(32)))) for _ in range(envs)])
+    done, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < budget_s:
+        ids = b.legal_action_ids_batch()
+        acts = np.array([int(x[rng.randrange(len(x))]) if len(x) else 0 for x in ids], np.int32)
+        done += int(np.asarray(b.step_batch(acts).valid).sum())
+    q.put((done, time.perf_counter() - t0, 0))
+
+
+def _junqi_core_worker(rank: int, envs: int, burn_in: int, budget_s: float, seed: int, q, seats: int = 1) -> None:
     """One host core's slice: the reference's own CPU path for one ply of the
     single-env rules (the JunqiEnv ply, GameState.step, state.py:626):
     acting-seat observation (ObservationBuilder.build_into, observation.py:
@@ -249,7 +269,8 @@ def _junqi_core_worker(rank: int, envs: int, burn_in: int, budget_s: float, seed
         done = 0
         for i, (g, bel) in enumerate(games):
             if obs:
-                builder.build_into(g, bel[g.turn.value], g.turn, sp, gl)
+                for s in ([g.turn] if seats == 1 else [Seat(k) for k in range(4)]):
+                    builder.build_into(g, bel[s.value], s, sp, gl)
             ids = g.legal_action_ids()
             if g.terminated or len(ids) == 0:
                 games[i] = fresh()
@@ -286,31 +307,40 @@ def reference_python_arm(args, cfg: dict) -> None:
         print(json.dumps({"impl": "reference-python", "unavailable": "baseline/_ref has no junqi_core; run "
                           "baseline/build_ref_cuda.py where the reference checkout exists"}), flush=True)
         return
-    if cfg["seats"] != 1:
-        print(json.dumps({"impl": "reference-python", "unavailable": "only the acting-seat configs are timed"}))
-        return
     cores = host_cores()
     per = 8
     burn = min(args.burn_in, 50)
+    seats = cfg["seats"]
     ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    procs = [ctx.Process(target=_junqi_core_worker, args=(r, per, burn, 20.0, args.seed, q)) for r in range(cores)]
-    for p in procs:
-        p.start()
-    res = [q.get(timeout=600) for _ in procs]
-    for p in procs:
-        p.join(timeout=60)
-    done = sum(r[0] for r in res)
-    secs = max(r[1] for r in res)
+
+    def run(target, nproc, head, tail=()):
+        """nproc processes of target(rank, *head, queue, *tail); (plies, seconds, per-process results)."""
+        q = ctx.Queue()
+        procs = [ctx.Process(target=target, args=(r, *head, q, *tail)) for r in range(nproc)]
+        for p in procs:
+            p.start()
+        res = [q.get(timeout=600) for _ in procs]
+        for p in procs:
+            p.join(timeout=60)
+        return sum(r[0] for r in res), max(r[1] for r in res), res
+
+    done, secs, res = run(_junqi_core_worker, cores, (per, burn, 20.0, args.seed), (seats,))
     rate = done / secs
+    what = "acting-seat observation" if seats == 1 else "observations of all 4 seats"
     sample = (f"{cores} processes x {per} envs, {min(r[2] for r in res)}-{max(r[2] for r in res)} plies each after "
-              f"a {burn}-ply burn-in, acting-seat observation + legal ids + step + 4-seat belief update, "
-              f"{secs:.1f} s")
+              f"a {burn}-ply burn-in, {what} + legal ids + step + 4-seat belief update, {secs:.1f} s")
+    # the vectorised step + legal path alone (no observation, no beliefs), 64 envs per process
+    one, one_s, _ = run(_batched_worker, 1, (64, 10.0, args.seed))
+    allc, all_s, _ = run(_batched_worker, cores, (64, 10.0, args.seed))
     print(json.dumps({"impl": "reference-python", "metric": "env plies/s (step + legal mask + 317-ch obs)",
                       "value": rate, "unit": "plies/s", "n_gpus": 1, "higher_is_better": True,
                       "config": arm_config(cfg, args, 1),
                       "cpu_baseline": {"value": rate, "unit": "plies/s", "cores": cores, "kind": "reference",
                                        "sample": sample},
+                      "step_legal_only": {"unit": "plies/s", "one_core": one / one_s, "all_cores": allc / all_s,
+                                          "cores": cores,
+                                          "sample": "BatchedGameState.step_batch + legal_action_ids_batch, 64 envs "
+                                                    "per process, uniform legal actions, 10 s"},
                       "source": "junqi_core (GameState.step, ObservationBuilder.build_into, BeliefTensor.update) "
                                 "from baseline/_ref"}), flush=True)
 
