@@ -223,21 +223,32 @@ def reference_arm(args, cfg: dict) -> None:
 def _batched_worker(rank: int, envs: int, budget_s: float, seed: int, q) -> None:
     """junqi_core's vectorised path on one core: BatchedGameState.step_batch
     (batched_state.py:417) + legal_action_ids_batch (:370) over `envs` games,
-    a uniform legal action each; finished games stay finished."""
+    a uniform legal action each.  The batch has no per-env reset, so games
+    are played in windows: a fresh batch, 50 untimed plies, then 300 timed
+    plies; windows repeat until the timed plies add up to budget_s."""
     import random
     sys.path.insert(0, str(ROOT / "baseline" / "_ref"))
     from junqi_core.batched_state import BatchedGameState
     from junqi_core.setup import generate_random_setup
     from junqi_core.state import GameState
     rng = random.Random(seed + 7919 * rank)
-    b = BatchedGameState.from_game_states(
-        [GameState.new_game(generate_random_setup(random.Random(rng.getrandbits(32)))) for _ in range(envs)])
-    done, t0 = 0, time.perf_counter()
-    while time.perf_counter() - t0 < budget_s:
+
+    def ply(b) -> int:
         ids = b.legal_action_ids_batch()
         acts = np.array([int(x[rng.randrange(len(x))]) if len(x) else 0 for x in ids], np.int32)
-        done += int(np.asarray(b.step_batch(acts).valid).sum())
-    q.put((done, time.perf_counter() - t0, 0))
+        return int(np.asarray(b.step_batch(acts).valid).sum())
+
+    done, secs = 0, 0.0
+    while secs < budget_s:
+        b = BatchedGameState.from_game_states(
+            [GameState.new_game(generate_random_setup(random.Random(rng.getrandbits(32)))) for _ in range(envs)])
+        for _ in range(50):
+            ply(b)
+        t0 = time.perf_counter()
+        for _ in range(300):
+            done += ply(b)
+        secs += time.perf_counter() - t0
+    q.put((done, secs, 0))
 
 
 def _junqi_core_worker(rank: int, envs: int, burn_in: int, budget_s: float, seed: int, q, seats: int = 1) -> None:
@@ -340,7 +351,8 @@ def reference_python_arm(args, cfg: dict) -> None:
                       "step_legal_only": {"unit": "plies/s", "one_core": one / one_s, "all_cores": allc / all_s,
                                           "cores": cores,
                                           "sample": "BatchedGameState.step_batch + legal_action_ids_batch, 64 envs "
-                                                    "per process, uniform legal actions, 10 s"},
+                                                    "per process, uniform legal actions, plies 50-349 of "
+                                                    "fresh games, >= 10 s timed"},
                       "source": "junqi_core (GameState.step, ObservationBuilder.build_into, BeliefTensor.update) "
                                 "from baseline/_ref"}), flush=True)
 
