@@ -42,20 +42,28 @@ enum : uint8_t { F_CAMP = 1, F_SH = 2, F_RAIL = 4, F_NINE = 8, F_ARC = 16, F_CUR
 // tracked type (idx+1), 14 uniform fallback, 32+slot prior of seat-local slot.
 enum : uint8_t { BC_NONE = 0, BC_UNIFORM = 14, BC_PRIOR0 = 32 };
 
-struct __align__(16) Topo {
+// The board tables the rules kernel reads; each of its CTAs holds a copy in
+// shared memory.
+struct __align__(16) TopoCore {
     int16_t c2f[NB];           // compact -> flat
     int16_t f2c[NC];           // flat -> compact, -1 off board
     uint8_t flags[NB];
     uint8_t curve[NB];         // legacy curve-rail id 0..4 (all cells carrying one)
     uint8_t adj4[NB][4];       // orthogonal neighbours (+x,-x,+y,-y)
     uint8_t diag[NB][4];       // diagonal steps into / out of a camp
-    uint8_t sray[NB][4][12];   // straight rail rays (+x,-x,+y,-y)
     uint8_t cray[NB][2][11];   // curve-chain rays (forward, backward)
     alignas(16) uint32_t railnb[NB][8];  // rail-graph neighbours as a mask; words NW.. are zero, so a
                                          // row loads as two 16-byte words
+    alignas(16) uint32_t ray[NB][4][NW];  // straight rail rays (+x,-x,+y,-y) as cell masks (build_ray_masks)
     uint8_t rot[4][NB];        // world compact -> canonical compact, per seat
-    int16_t rotf[4][NC];       // world flat -> canonical flat, per seat
     uint8_t slot_cell[4][30];  // compact cell of (seat, slot)
+};
+
+// All board tables: the rules kernel's, and those only the host, the
+// observation encoder and the 80-slot mask read.
+struct __align__(16) Topo : TopoCore {
+    uint8_t sray[NB][4][12];   // straight rail rays (+x,-x,+y,-y) as cell lists
+    int16_t rotf[4][NC];       // world flat -> canonical flat, per seat
     int8_t slot_ch[30];        // piece-slot channel of a seat-local slot, -1 camp
 };
 

@@ -349,17 +349,12 @@ int jq_init(int device) {
     static bool built = false;
     if (!built) {
         build_topo(host_topo);
+        if (!build_ray_masks(host_topo, host_topo.ray)) return fail(JQ_ERR_ARG, "straight rail rays out of order");
         build_slot_topo(host_topo, host_slot);
         built = true;
     }
-    CU(cudaMemcpyToSymbol(c_topo, &host_topo, sizeof(Topo)));
     CU(cudaMemcpyToSymbol(g_topo, &host_topo, sizeof(Topo)));
     CU(cudaMemcpyToSymbol(g_slot, &host_slot, sizeof(SlotTopo)));
-    {
-        static uint32_t rays[NB][4][NW];
-        if (!build_ray_masks(host_topo, rays)) return fail(JQ_ERR_ARG, "straight rail rays out of order");
-        CU(cudaMemcpyToSymbol(g_ray, rays, sizeof(rays)));
-    }
     {
         static uint32_t statw[4][4][STAT_WORDS];
         build_static_words(host_topo, statw);

@@ -12,7 +12,7 @@ constexpr int RULE_THREADS = RULE_WARPS * 32;
 enum : int { DO_STEP = 1, DO_RESET = 2, DO_LEGAL = 4, RESET_ALL = 8, DO_BELIEF_INIT = 16 };
 
 struct RuleSmem {
-    Topo topo;
+    TopoCore topo;
     WEnv w[RULE_WARPS];
     int applied;  // plies applied by this CTA (statistics)
 };
@@ -41,19 +41,18 @@ __device__ __forceinline__ int pool_index(uint64_t seed, uint64_t ply, int e, in
     return (int)(hash3(seed, ply, (uint64_t)e) % (uint64_t)P);
 }
 
-// The board tables into shared memory, 16 bytes per thread and step.
-__device__ __forceinline__ void stage_topo(Topo &dst_t, int tid, int nthreads) {
-    const uint4 *src = reinterpret_cast<const uint4 *>(&g_topo);
+// The rules kernel's board tables into shared memory, 16 bytes per thread
+// and step.
+static_assert(sizeof(TopoCore) % 16 == 0, "TopoCore copies in 16-byte words");
+__device__ __forceinline__ void stage_topo(TopoCore &dst_t, int tid, int nthreads) {
+    const uint4 *src = reinterpret_cast<const uint4 *>(static_cast<const TopoCore *>(&g_topo));
     uint4 *dst = reinterpret_cast<uint4 *>(&dst_t);
-    for (int k = tid; k < (int)(sizeof(Topo) / 16); k += nthreads) dst[k] = src[k];
-    const unsigned char *s8 = reinterpret_cast<const unsigned char *>(&g_topo);
-    unsigned char *d8 = reinterpret_cast<unsigned char *>(&dst_t);
-    for (int k = (int)(sizeof(Topo) / 16) * 16 + tid; k < (int)sizeof(Topo); k += nthreads) d8[k] = s8[k];
+    for (int k = tid; k < (int)(sizeof(TopoCore) / 16); k += nthreads) dst[k] = src[k];
 }
 
 // The parts of a ply `a.flags` selects, for env e, by one warp.  Returns (on
 // every lane) whether a step was applied.
-__device__ bool warp_ply_env(const RuleArgs &a, const Topo &T, WEnv &w, int e, int lane) {
+__device__ bool warp_ply_env(const RuleArgs &a, const TopoCore &T, WEnv &w, int e, int lane) {
     const jq_batch &b = a.b;
     bool applied = false;
     const bool traced = threadIdx.x == 0 && e < RULE_WARPS * (int)gridDim.x;  // warp 0's first env

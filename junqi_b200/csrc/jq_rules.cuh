@@ -30,14 +30,12 @@ constexpr unsigned FULL = 0xffffffffu;
 // ---------------------------------------------------------------------------
 // Device tables (filled by the host API, see jq_api.cu)
 // ---------------------------------------------------------------------------
-__constant__ Topo c_topo;
 __device__ Topo g_topo;  // same tables in global memory, for per-lane (divergent) reads
 __constant__ int64_t c_zturn[4], c_zwin[3], c_zsdead[4], c_zsflag[4], c_zshow[4];
 __constant__ int64_t c_zterm, c_zdraw;
 __device__ int64_t g_zpiece[NP * 14 * NC];
 __device__ int64_t g_zmc[4096];
 __device__ int64_t g_zmslc[512];
-__device__ uint32_t g_ray[NB][4][NW];  // straight rail rays as cell masks (build_ray_masks)
 __device__ float g_prior[30 * 12];
 __device__ float g_uniform[12];
 __device__ float g_recency[4 * RECENCY_LEN];
@@ -100,7 +98,7 @@ __device__ __forceinline__ size_t OI(int e, int o, int p) { return ((size_t)e * 
 // Every load is issued before any shared-memory store, so the warp waits
 // for global memory once.  with_bel: also the env's 480 belief codes, read
 // and rewritten by the step's belief update.
-__device__ void warp_load(const jq_batch &b, const Topo &T, WEnv &w, int e, int lane, bool with_bel) {
+__device__ void warp_load(const jq_batch &b, const TopoCore &T, WEnv &w, int e, int lane, bool with_bel) {
     constexpr int CI = (NC + 31) / 32, PIT = (NP + 31) / 32;
     int cp[CI];
 #pragma unroll
@@ -174,7 +172,7 @@ __device__ void warp_load(const jq_batch &b, const Topo &T, WEnv &w, int e, int 
 // ---------------------------------------------------------------------------
 // Destination mask of one piece standing on compact cell c (move_gen.py:
 // 1311-1553 restricted to one candidate piece).
-__device__ void piece_dsts(const Topo &T, int c, int t, const uint32_t (&empty)[NW], const uint32_t (&land)[NW],
+__device__ void piece_dsts(const TopoCore &T, int c, int t, const uint32_t (&empty)[NW], const uint32_t (&land)[NW],
                            uint32_t (&out)[NW]) {
 #pragma unroll
     for (int i = 0; i < NW; ++i) out[i] = 0;
@@ -236,7 +234,7 @@ __device__ void piece_dsts(const Topo &T, int c, int t, const uint32_t (&empty)[
         for (int k = 0; k < 4; ++k) {
             uint32_t r[NW];
 #pragma unroll
-            for (int i = 0; i < NW; ++i) r[i] = __ldg(&g_ray[c][k][i]);
+            for (int i = 0; i < NW; ++i) r[i] = T.ray[c][k][i];
             int stop = (k & 1) ? -1 : (1 << 20);  // no blocker: the whole ray
 #pragma unroll
             for (int i = 0; i < NW; ++i) {
@@ -263,7 +261,7 @@ __device__ void piece_dsts(const Topo &T, int c, int t, const uint32_t (&empty)[
     }
 }
 
-__device__ __forceinline__ void board_masks(const Topo &T, const WEnv &w, int lane, int team, uint32_t *empty,
+__device__ __forceinline__ void board_masks(const TopoCore &T, const WEnv &w, int lane, int team, uint32_t *empty,
                                             uint32_t *land) {
 #pragma unroll
     for (int i = 0; i < NW; ++i) {
@@ -289,7 +287,7 @@ __device__ __forceinline__ int lane_source(const WEnv &w, int lane, int seat) {
 
 // has_legal_moves_soa (move_gen.py:1557-1609): any legal action for `seat`,
 // ignoring terminated / dead flags.
-__device__ bool warp_has_moves(const Topo &T, const WEnv &w, int lane, int seat, int *full_scans = nullptr) {
+__device__ bool warp_has_moves(const TopoCore &T, const WEnv &w, int lane, int seat, int *full_scans = nullptr) {
     uint32_t empty[NW], land[NW], d[NW];
     board_masks(T, w, lane, seat & 1, empty, land);
     int src = lane_source(w, lane, seat);
@@ -331,7 +329,7 @@ __device__ __forceinline__ uint4 mask_chunk(const WEnv &w, int j0) {
 // Legal actions of `seat` (empty when `skip`), ascending, written to ids
 // (up to cap); optional canonical (16641) byte mask.  Returns the count on
 // every lane.
-__device__ int warp_legal(const Topo &T, WEnv &w, int lane, int seat, bool skip, int32_t *ids, int cap,
+__device__ int warp_legal(const TopoCore &T, WEnv &w, int lane, int seat, bool skip, int32_t *ids, int cap,
                           uint8_t *mask_env, bool traced = false) {
     uint32_t empty[NW], land[NW], d[NW] = {0, 0, 0, 0, 0};
     board_masks(T, w, lane, seat & 1, empty, land);
@@ -410,9 +408,9 @@ __device__ int warp_legal(const Topo &T, WEnv &w, int lane, int seat, bool skip,
 }
 
 // ---------------------------------------------------------------------------
-// Path-revealed engineer (move_gen.py:245-296) on the pre-move board, scalar
+// Path-revealed engineer (move_gen.py:245-296) on the pre-move board
 // ---------------------------------------------------------------------------
-__device__ bool ray_clear_to(const Topo &T, const WEnv &w, const uint8_t *ray, int n, int dst) {
+__device__ bool ray_clear_to(const TopoCore &T, const WEnv &w, const uint8_t *ray, int n, int dst) {
     for (int l = 0; l < n; ++l) {
         int nb = ray[l];
         if (nb == NONE8) return false;
@@ -423,33 +421,34 @@ __device__ bool ray_clear_to(const Topo &T, const WEnv &w, const uint8_t *ray, i
 }
 
 // Whether an engineer on compact cell s reaches d along the railway through
-// empty cells (move_gen.py:186-224), by the whole warp (the result on every
-// lane): lane l tests cells l, l + 32, ... for a rail neighbour in the
-// frontier (the rail graph is symmetric), and one ballot per mask word
-// gathers the next frontier, so an expansion costs a few shared loads per
-// lane instead of one lane's serial walk over the frontier's neighbours.
-__device__ bool warp_engineer_reach(const Topo &T, const WEnv &w, int lane, int s, int d) {
-    if (!(T.flags[s] & F_RAIL) || !(T.flags[d] & F_RAIL) || s == d) return false;
-    uint32_t empty[NW], reach[NW] = {0, 0, 0, 0, 0}, fr[NW] = {0, 0, 0, 0, 0};
-#pragma unroll
-    for (int i = 0; i < NW; ++i) {
-        const int c = i * 32 + lane;
-        empty[i] = __ballot_sync(FULL, c < NB && w.cell[T.c2f[c]] < 0);
-    }
+// the empty cells `empty` (move_gen.py:186-224), by the whole warp (the
+// result on every lane): the frontier's rail neighbours are the union of its
+// cells' rows of railnb; lane l ORs the rows of the frontier cells l, l + 32,
+// ... (a frontier holds a few cells, so most lanes load nothing) and one OR
+// reduction per mask word gathers the union on every lane.
+__device__ bool warp_engineer_reach(const TopoCore &T, int lane, int s, int d, const uint32_t (&empty)[NW],
+                                    int *rounds = nullptr) {
+    uint32_t reach[NW] = {0, 0, 0, 0, 0}, fr[NW] = {0, 0, 0, 0, 0};
     rset(reach, s);
     rset(fr, s);
     for (int it = 0; it < NB; ++it) {
-        uint32_t nbm[NW];
+#ifdef JQ_TRACE
+        if (rounds) *rounds = it + 1;
+#endif
+        uint32_t nbm[NW] = {0, 0, 0, 0, 0};
 #pragma unroll
-        for (int i = 0; i < NW; ++i) {
-            const int c = i * 32 + lane;
-            bool hit = false;
-            if (c < NB)
+        for (int i = 0; i < NW; ++i)
+            if ((fr[i] >> lane) & 1u) {  // frontier bits are cells < NB
+                const uint4 *row = reinterpret_cast<const uint4 *>(T.railnb[i * 32 + lane]);
+                const uint4 r0 = row[0], r1 = row[1];
+                nbm[0] |= r0.x;
+                nbm[1] |= r0.y;
+                nbm[2] |= r0.z;
+                nbm[3] |= r0.w;
+                nbm[4] |= r1.x;
+            }
 #pragma unroll
-                for (int k = 0; k < NW; ++k)
-                    if (fr[k]) hit |= (T.railnb[c][k] & fr[k]) != 0u;  // fr is the same on every lane
-            nbm[i] = __ballot_sync(FULL, hit);
-        }
+        for (int i = 0; i < NW; ++i) nbm[i] = __reduce_or_sync(FULL, nbm[i]);
         if (rbit(nbm, d)) return true;
         uint32_t any = 0;
 #pragma unroll
@@ -464,7 +463,28 @@ __device__ bool warp_engineer_reach(const Topo &T, const WEnv &w, int lane, int 
     return false;
 }
 
-__device__ bool move_requires_gongb(const Topo &T, const WEnv &w, int sf, int df, int lane) {
+// Whether d lies on straight rail ray k of s with every ray cell before it
+// empty.  The ray's cells increase (k even) or decrease (k odd) in compact
+// order, so the cells before d are the ray's cells below (above) d.
+__device__ __forceinline__ bool ray_clear_mask(const TopoCore &T, int s, int k, int d, const uint32_t (&empty)[NW]) {
+    bool on = false, blocked = false;
+#pragma unroll
+    for (int i = 0; i < NW; ++i) {
+        const uint32_t r = T.ray[s][k][i];
+        const int lim = d - i * 32;
+        const uint32_t below = lim <= 0 ? 0u : (lim >= 32 ? ~0u : (1u << lim) - 1u);
+        const uint32_t dbit = (lim >= 0 && lim < 32) ? 1u << lim : 0u;
+        const uint32_t before = (k & 1) ? ~(below | dbit) : below;
+        on |= (r & dbit) != 0u;
+        blocked |= (r & ~empty[i] & before) != 0u;
+    }
+    return on && !blocked;
+}
+
+// move_gen.py:245-296: whether the move sf -> df is one only an engineer's
+// rail run makes.  Called by the whole warp (the board's empty cells are one
+// ballot per mask word); the result is the same on every lane.
+__device__ bool move_requires_gongb(const TopoCore &T, const WEnv &w, int sf, int df, int lane, int *rounds = nullptr) {
     if (sf == df) return false;
     int sx = sf % 17, sy = sf / 17, dx = df % 17, dy = df / 17;
     int adx = abs(sx - dx), ady = abs(sy - dy);
@@ -473,16 +493,23 @@ __device__ bool move_requires_gongb(const Topo &T, const WEnv &w, int sf, int df
     if (adx + ady == 1) return false;
     if (adx == 1 && ady == 1 && ((T.flags[s] & F_CAMP) || (T.flags[d] & F_CAMP))) return false;
     if (!(T.flags[s] & F_RAIL) || !(T.flags[d] & F_RAIL)) return false;
+    uint32_t empty[NW];
+#pragma unroll
+    for (int i = 0; i < NW; ++i) {
+        const int c = i * 32 + lane;
+        empty[i] = __ballot_sync(FULL, c < NB && w.cell[T.c2f[c]] < 0);
+    }
     if (sx == dx || sy == dy) {
-        for (int k = 0; k < 4; ++k)
-            if (ray_clear_to(T, w, T.sray[s][k], 12, d)) return false;
-        return warp_engineer_reach(T, w, lane, s, d);
+        // a straight run: only the ray pointing at d can hold it
+        const int k = sy == dy ? (dx > sx ? 0 : 1) : (dy > sy ? 2 : 3);
+        if (ray_clear_mask(T, s, k, d, empty)) return false;
+        return warp_engineer_reach(T, lane, s, d, empty, rounds);
     }
     if (T.curve[s] > 0 && T.curve[s] == T.curve[d] && (T.flags[s] & F_CURVE_ACTIVE)) {
         for (int k = 0; k < 2; ++k)
             if (ray_clear_to(T, w, T.cray[s][k], 11, d)) return false;
     }
-    return warp_engineer_reach(T, w, lane, s, d);
+    return warp_engineer_reach(T, lane, s, d, empty, rounds);
 }
 
 // ---------------------------------------------------------------------------
@@ -628,7 +655,7 @@ __device__ __forceinline__ bool sees_truth(int obs, int owner, int mode) {
 }
 __device__ __forceinline__ bool bc_onehot(int c) { return c >= 1 && c <= 12; }
 
-__device__ __forceinline__ uint8_t initial_code(const Topo &T, const WEnv &w, int o, int p, int mode) {
+__device__ __forceinline__ uint8_t initial_code(const TopoCore &T, const WEnv &w, int o, int p, int mode) {
     if (!w.alive[p]) return BC_NONE;
     int s = w.seat[p];
     if (sees_truth(o, s, mode)) return (uint8_t)(tracked_idx(w.type[p]) + 1);
@@ -642,7 +669,7 @@ __device__ __forceinline__ uint8_t initial_code(const Topo &T, const WEnv &w, in
     return BC_UNIFORM;
 }
 
-__device__ void warp_belief_init(const jq_batch &b, const Topo &T, WEnv &w, int e, int lane, int mode) {
+__device__ void warp_belief_init(const jq_batch &b, const TopoCore &T, WEnv &w, int e, int lane, int mode) {
     for (int k = lane; k < 4 * NP; k += 32) {
         int o = k / NP, p = k - o * NP;
         const uint8_t c = initial_code(T, w, o, p, mode);
@@ -683,7 +710,7 @@ __device__ __forceinline__ bool rem_untrack(WEnv &w, int o, int seat) {
 // Lane o (0..3) applies R3, R5/R7, R4/R6, R1 and R9 for observer o; then the
 // whole warp runs the I5 sweep.  The codes are the shared-memory copy
 // warp_load took; chunks the rules change are written back.
-__device__ void warp_belief_update(const jq_batch &b, const Topo &T, WEnv &w, int e, int lane,
+__device__ void warp_belief_update(const jq_batch &b, const TopoCore &T, WEnv &w, int e, int lane,
                                    const StepCtx &x, int mode, const int *died) {
     bool touched = false;  // R-rules rewrote a code of this lane's observer
     bool inv = false;      // ... or an inventory entry
@@ -795,7 +822,7 @@ __device__ void warp_belief_update(const jq_batch &b, const Topo &T, WEnv &w, in
 // Seat surrender (batched_state.py:1078-1121), warp-parallel; returns the
 // Zobrist delta on every lane.
 // ---------------------------------------------------------------------------
-__device__ int64_t warp_surrender(const jq_batch &b, const Topo &T, WEnv &w, int e, int lane, int seat, int step) {
+__device__ int64_t warp_surrender(const jq_batch &b, const TopoCore &T, WEnv &w, int e, int lane, int seat, int step) {
     int64_t d = 0;
     const bool keep_loc = b.rules == JQ_RULES_GAMESTATE;  // state.py:640-693 records the current cell
     for (int p = lane; p < NP; p += 32) {
@@ -830,7 +857,7 @@ __device__ int64_t warp_surrender(const jq_batch &b, const Topo &T, WEnv &w, int
 // ---------------------------------------------------------------------------
 // Reset to GameState.new_game(lineup) (state.py:490-624), warp-parallel
 // ---------------------------------------------------------------------------
-__device__ void warp_reset(const jq_batch &b, const Topo &T, WEnv &w, int e, int lane, const int8_t *lineup, int mode) {
+__device__ void warp_reset(const jq_batch &b, const TopoCore &T, WEnv &w, int e, int lane, const int8_t *lineup, int mode) {
     for (int f = lane; f < NC; f += 32) {
         w.cell[f] = -1;
         b.cell_pid[(size_t)e * NC + f] = -1;
@@ -920,7 +947,7 @@ __device__ __forceinline__ void check_victory(const WEnv &w, int acting, int mc,
     if (mc >= 4000 || mslc >= 200) { term = 1; draw = 1; }
 }
 
-__device__ __forceinline__ void kill_piece(const jq_batch &b, const Topo &T, WEnv &w, int e, int pid, int cell_f,
+__device__ __forceinline__ void kill_piece(const jq_batch &b, const TopoCore &T, WEnv &w, int e, int pid, int cell_f,
                                            int reason, int step, int loc) {
     if (!w.alive[pid]) return;
     size_t q = PI(e, pid);
@@ -936,7 +963,7 @@ __device__ __forceinline__ void kill_piece(const jq_batch &b, const Topo &T, WEn
     b.death_loc[q] = (int16_t)loc;
 }
 
-__device__ __forceinline__ void move_piece(const jq_batch &b, const Topo &T, WEnv &w, int e, int pid, int sf, int df) {
+__device__ __forceinline__ void move_piece(const jq_batch &b, const TopoCore &T, WEnv &w, int e, int pid, int sf, int df) {
     size_t q = PI(e, pid);
     w.cell[sf] = -1;
     w.cell[df] = (int16_t)pid;
@@ -948,7 +975,7 @@ __device__ __forceinline__ void move_piece(const jq_batch &b, const Topo &T, WEn
 }
 
 // Returns true on every lane when the ply was applied.
-__device__ bool warp_step(const jq_batch &b, const Topo &T, WEnv &w, int e, int lane, int32_t act, int mode,
+__device__ bool warp_step(const jq_batch &b, const TopoCore &T, WEnv &w, int e, int lane, int32_t act, int mode,
                           const jq_step_out &out, int64_t *stats, bool traced = false) {
     StepCtx &x = w.x;
     int64_t zob = 0;
@@ -980,9 +1007,15 @@ __device__ bool warp_step(const jq_batch &b, const Topo &T, WEnv &w, int e, int 
     // path-revealed engineer (move_gen.py:245-296) on the pre-move board, by
     // the whole warp: a move only an engineer's rail run can make
     bool gongb_path = false;
+    int path_rounds = 0;
     if (x.A_type == GONGB) {
         const int adx = abs(x.sf % 17 - x.df % 17), ady = abs(x.sf / 17 - x.df / 17);
-        if (x.D >= 0 || adx + ady > 1) gongb_path = move_requires_gongb(T, w, x.sf, x.df, lane);
+        if (x.D >= 0 || adx + ady > 1) gongb_path = move_requires_gongb(T, w, x.sf, x.df, lane, &path_rounds);
+    }
+    if (traced) {
+        JQ_TRACE_AT(1, TR_PATH);
+        JQ_TRACE_COUNT(1, TR_PATH_ROUNDS, path_rounds);
+        JQ_TRACE_COUNT(1, TR_ATYPE, x.A_type);
     }
     if (lane == 0) {
         const int sf = x.sf, df = x.df, A = x.A, D = x.D;

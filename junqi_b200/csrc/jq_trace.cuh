@@ -14,7 +14,7 @@ namespace jq {
 
 constexpr int TRACE_KERNELS = 2;   // 0: obs_kernel, 1: rules_kernel
 constexpr int TRACE_CTAS = 1024;   // CTAs recorded per launch (grid beyond this is not traced)
-constexpr int TRACE_POINTS = 16;
+constexpr int TRACE_POINTS = 20;
 
 // obs_kernel points
 enum : int { TO_ENTRY = 0, TO_WAITED = 1, TO_FIRST_STAGED = 2, TO_FIRST_STREAM = 3, TO_LAST_STREAMED = 4,
@@ -27,7 +27,9 @@ enum : int { TR_ENTRY = 0, TR_WAITED = 1, TR_LOADED = 2, TR_STEPPED = 3, TR_RESE
              // counts: the env's event (0: no step), Q12 full destination scans
              TR_EVENT = 12, TR_Q12_SCANS = 13,
              // inside legal generation: destination sets done, ranking and scan done
-             TR_DSTS = 14, TR_RANKED = 15 };
+             TR_DSTS = 14, TR_RANKED = 15,
+             // inside the step: the engineer path check done, its rounds (0: not run), the moving piece's type
+             TR_PATH = 16, TR_PATH_ROUNDS = 17, TR_ATYPE = 18 };
 
 #ifdef JQ_TRACE
 __device__ uint64_t g_trace[TRACE_KERNELS][TRACE_CTAS][TRACE_POINTS];

@@ -26,7 +26,7 @@ from . import _native as N
 OBS, RULES = 0, 1
 
 
-POINTS = 16
+POINTS = 20
 
 
 def read(kernel: int, ctas: int) -> np.ndarray:
@@ -97,7 +97,21 @@ def rules_timeline(t: np.ndarray) -> dict:
                        "beliefs": round((t[i, 3] - t[i, 11]) / 1e3, 1), "ids": round((t[i, 5] - t[i, 4]) / 1e3, 1),
                        "dsts": round((t[i, 14] - t[i, 4]) / 1e3, 1), "rank": round((t[i, 15] - t[i, 14]) / 1e3, 1),
                        "mask": round((t[i, 6] - t[i, 5]) / 1e3, 1), "event": int(t[i, 12]),
-                       "q12_scans": int(t[i, 13])} for i in slow]
+                       "q12_scans": int(t[i, 13]), "path": round((t[i, 16] - t[i, 2]) / 1e3, 1),
+                       "path_rounds": int(t[i, 17]), "piece_type": int(t[i, 18])} for i in slow]
+    # the engineer path check: how many envs ran it, its rounds and time, and
+    # the scalar part with and without it
+    ran = t[:, 17] > 0
+    path = (t[:, 16] - t[:, 2]) / 1e3
+    scal = (t[:, 8] - t[:, 2]) / 1e3
+    out["path_check"] = {"envs": int(ran.sum()), "of": int(len(t)),
+                         "rounds_p50_max": [int(np.median(t[ran, 17])), int(t[ran, 17].max())] if ran.any() else [],
+                         "us_p50_max": [round(float(np.median(path[ran])), 2), round(float(path[ran].max()), 2)]
+                         if ran.any() else [],
+                         "scalar_us_with_p50_max": [round(float(np.median(scal[ran])), 2), round(float(scal[ran].max()), 2)]
+                         if ran.any() else [],
+                         "scalar_us_without_p50_max": [round(float(np.median(scal[~ran])), 2),
+                                                       round(float(scal[~ran].max()), 2)]}
     return out
 
 
