@@ -337,6 +337,16 @@ __device__ int warp_legal(const TopoCore &T, WEnv &w, int lane, int seat, bool s
     if (src >= 0) piece_dsts(T, src, w.type[seat * 30 + lane], empty, land, d);
     int cnt = __popc(d[0]) + __popc(d[1]) + __popc(d[2]) + __popc(d[3]) + __popc(d[4]);
     if (traced) JQ_TRACE_AT(1, TR_DSTS);  // lane 0 only: no warp barrier here
+#ifdef JQ_TRACE
+    {  // every lane: the warp reductions stay outside the lane-0 block
+        const bool eng = src >= 0 && w.type[seat * 30 + lane] == GONGB;
+        const uint64_t ne = __popc(__ballot_sync(FULL, eng));
+        const uint64_t em = __reduce_max_sync(FULL, eng ? (unsigned)cnt : 0u);
+        const uint64_t cm = __reduce_max_sync(FULL, (unsigned)cnt);
+        const uint64_t tot = __reduce_add_sync(FULL, (unsigned)cnt);
+        if (traced) JQ_TRACE_COUNT(1, TR_LEGAL_SHAPE, (ne << 48) | (em << 32) | (cm << 16) | tot);
+    }
+#endif
     // rank of the source among all sources (compact order == flat order)
     int rank = 0;
 #pragma unroll

@@ -29,7 +29,9 @@ enum : int { TR_ENTRY = 0, TR_WAITED = 1, TR_LOADED = 2, TR_STEPPED = 3, TR_RESE
              // inside legal generation: destination sets done, ranking and scan done
              TR_DSTS = 14, TR_RANKED = 15,
              // inside the step: the engineer path check done, its rounds (0: not run), the moving piece's type
-             TR_PATH = 16, TR_PATH_ROUNDS = 17, TR_ATYPE = 18 };
+             TR_PATH = 16, TR_PATH_ROUNDS = 17, TR_ATYPE = 18,
+             // the legal set's shape: engineers, their largest destination count, any piece's largest, total
+             TR_LEGAL_SHAPE = 19 };
 
 #ifdef JQ_TRACE
 __device__ uint64_t g_trace[TRACE_KERNELS][TRACE_CTAS][TRACE_POINTS];

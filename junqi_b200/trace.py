@@ -98,7 +98,22 @@ def rules_timeline(t: np.ndarray) -> dict:
                        "dsts": round((t[i, 14] - t[i, 4]) / 1e3, 1), "rank": round((t[i, 15] - t[i, 14]) / 1e3, 1),
                        "mask": round((t[i, 6] - t[i, 5]) / 1e3, 1), "event": int(t[i, 12]),
                        "q12_scans": int(t[i, 13]), "path": round((t[i, 16] - t[i, 2]) / 1e3, 1),
-                       "path_rounds": int(t[i, 17]), "piece_type": int(t[i, 18])} for i in slow]
+                       "path_rounds": int(t[i, 17]), "piece_type": int(t[i, 18]),
+                       "legal": _legal_shape(t[i, 19])} for i in slow]
+    # destination-set time against the legal set's shape
+    dst = (t[:, 14] - t[:, 4]) / 1e3
+    shape = [_legal_shape(v) for v in t[:, 19]]
+    tot = np.array([s["total"] for s in shape])
+    eng = np.array([s["engineer_max"] for s in shape])
+    out["legal_dsts_by_shape"] = {
+        "total_moves_p50_max": [int(np.median(tot)), int(tot.max())],
+        "corr_dsts_total": round(float(np.corrcoef(dst, tot)[0, 1]), 2) if tot.std() > 0 else None,
+        "corr_dsts_engineer_max": round(float(np.corrcoef(dst, eng)[0, 1]), 2) if eng.std() > 0 else None,
+        "dsts_us_p50_by_total_quartile": [round(float(np.median(dst[(tot >= a) & (tot <= b)])), 2)
+                                          for a, b in zip(np.percentile(tot, [0, 25, 50, 75]),
+                                                          np.percentile(tot, [25, 50, 75, 100]))],
+        "dsts_us_p50_engineer_max_ge_20_vs_lt": [round(float(np.median(dst[eng >= 20])), 2) if (eng >= 20).any() else None,
+                                                 round(float(np.median(dst[eng < 20])), 2) if (eng < 20).any() else None]}
     # the engineer path check: how many envs ran it, its rounds and time, and
     # the scalar part with and without it
     ran = t[:, 17] > 0
@@ -113,6 +128,13 @@ def rules_timeline(t: np.ndarray) -> dict:
                          "scalar_us_without_p50_max": [round(float(np.median(scal[~ran])), 2),
                                                        round(float(scal[~ran].max()), 2)]}
     return out
+
+
+def _legal_shape(v) -> dict:
+    """The packed legal-set shape of one traced env (tracing build)."""
+    v = int(v)
+    return {"engineers": v >> 48, "engineer_max": (v >> 32) & 0xFFFF, "piece_max": (v >> 16) & 0xFFFF,
+            "total": v & 0xFFFF}
 
 
 def sweep() -> None:
