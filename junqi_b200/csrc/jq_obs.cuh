@@ -108,6 +108,8 @@ struct __align__(16) UnitBuf {
     uint8_t pbase[NP], pcode[NP];       // belief record: first plane (12 / 27 / 39) and belief code
     float pbel[NP][12];                 // belief record with caller-given beliefs: the 12 values at the cell
     uint8_t bel_list[NP], cm_list[NP];  // pids holding a belief / combat-memory record
+    int32_t bel_off[NP];                // belief record j (list order): output float of its plane-0 value
+    uint8_t bel_row[NP];                // belief record j: its row of ObsSmem::bel_tab
     int nbel, ncm;
     int32_t exc_pos[EXC_MAX];           // output float index of each exception
     float exc_val[EXC_MAX];
@@ -122,7 +124,9 @@ struct __align__(16) ObsSmem {
     int16_t rotf[4][NC];                // world flat -> canonical flat, per observer seat
     uint32_t statw[4][4][STAT_WORDS];   // board-static bits as stream words, per observer and stream offset
     int ticket[1], next_o[1];  // the staging warps' next unit and its observer
-    float prior[30 * 12], uniform[12];  // belief tables: global loads here would wait behind the write stream
+    // belief values: rows 0..29 the prior of a seat-local slot, row 30 the
+    // uniform fallback (global loads here would wait behind the write stream)
+    float bel_tab[31 * 12];
     int8_t slot_ch[30];
 };
 
@@ -137,13 +141,6 @@ __device__ __forceinline__ bool in_back_two(int seat, int zx, int zy) {
     case 3: return zx >= 15 && zx <= 16;
     }
     return false;
-}
-
-__device__ __forceinline__ float bel_value(const float *prior, const float *uniform, int code, int t) {
-    if (code >= 1 && code <= 12) return code - 1 == t ? 1.f : 0.f;
-    if (code == BC_UNIFORM) return uniform[t];
-    if (code >= BC_PRIOR0 && code < BC_PRIOR0 + 30) return prior[(code - BC_PRIOR0) * 12 + t];
-    return 0.f;
 }
 
 __device__ __forceinline__ void set_bit(uint32_t *s, int q) { atomicOr(&s[q >> 5], 1u << (q & 31)); }
@@ -284,7 +281,13 @@ __device__ void stage_piece(const jq_batch &b, int e, int o, int mode, const Obs
         if (s == left) { st.one(25, cell); base = 27; }
         if (s == right) { st.one(26, cell); base = 39; }
         uint32_t flag = 0;
-        if (base >= 0) {  // belief planes: expanded from this record by the streaming warps
+        // belief planes: a one-hot code (a known type) is a 1.0 among 0.0s,
+        // so a bit of the stream; a prior or uniform code is a record the
+        // streaming warps expand (any other code lights nothing); caller-given
+        // beliefs are always records
+        const bool bel_rec = st.ext || code == BC_UNIFORM || (code >= BC_PRIOR0 && code < BC_PRIOR0 + 30);
+        if (base >= 0 && !st.ext && code >= 1 && code <= 12) st.one(base + code - 1, cell);
+        if (base >= 0 && bel_rec) {
             flag = 1;
             st.B.pbase[p] = (uint8_t)base;
             st.B.pcode[p] = (uint8_t)code;
@@ -426,7 +429,12 @@ __device__ void stage_unit(const jq_batch &b, int seats, int mode, const float *
         }
         bb = __shfl_sync(0xffffffffu, bb, 0);
         bc = __shfl_sync(0xffffffffu, bc, 0);
-        if (fl & 1u) B.bel_list[bb + __popc(mb & below)] = (uint8_t)p;
+        if (fl & 1u) {
+            const int j = bb + __popc(mb & below), code = B.pcode[p];
+            B.bel_list[j] = (uint8_t)p;
+            B.bel_off[j] = B.pbase[p] * NC + B.pcell[p];
+            B.bel_row[j] = (uint8_t)(code == BC_UNIFORM ? 30 : code - BC_PRIOR0);
+        }
         if (fl & 2u) B.cm_list[bc + __popc(mc & below)] = (uint8_t)p;
     }
     if (t < HIST) {  // move history (observation.py:1207-1231)
@@ -465,7 +473,7 @@ __device__ void stage_unit(const jq_batch &b, int seats, int mode, const float *
 
 // Streaming warps: write unit B.u.  w = streaming warp 0..nwarps-1, t = its thread;
 // bar_stream is a named barrier of the nwarps streaming warps.
-__device__ void stream_unit(UnitBuf &B, const float *prior, const float *uniform, bool ext, float *spatial,
+__device__ void stream_unit(UnitBuf &B, const float *bel_tab, bool ext, float *spatial,
                             float *global, int w, int lane, int nwarps, int bar_stream) {
     const int u = B.u, t = w * 32 + lane;
     float *out = spatial + (size_t)u * OBS_FLOATS;
@@ -499,10 +507,10 @@ __device__ void stream_unit(UnitBuf &B, const float *prior, const float *uniform
     for (int i = t; i < n; i += nthr) out[B.exc_pos[i]] = B.exc_val[i];
     const int nb = B.nbel * 12, nc = B.ncm * 16;
     for (int i = t; i < nb; i += nthr) {
-        const int j = i / 12, k = i - j * 12, p = B.bel_list[j];
+        const int j = i / 12, k = i - j * 12;
         // caller-given beliefs are written where > 0 (observation.cu:330-370)
-        const float v = ext ? B.pbel[p][k] : bel_value(prior, uniform, B.pcode[p], k);
-        if (v > 0.f) out[(B.pbase[p] + k) * NC + B.pcell[p]] = v;
+        const float v = ext ? B.pbel[B.bel_list[j]][k] : bel_tab[B.bel_row[j] * 12 + k];
+        if (v > 0.f) out[B.bel_off[j] + k * NC] = v;
     }
     if (ext && t < 24) {
         // global[0:24] from caller-given beliefs: their sums over the left /
@@ -548,8 +556,8 @@ __global__ void __launch_bounds__(OBS_THREADS, OBS_MIN_CTAS) obs_kernel(jq_batch
     // once per CTA: observer rotations, belief tables and board-static words
     // into shared memory; both bitstreams cleared
     for (int i = tid; i < 4 * NC; i += OBS_THREADS) (&S.rotf[0][0])[i] = (&g_topo.rotf[0][0])[i];
-    for (int i = tid; i < 30 * 12; i += OBS_THREADS) S.prior[i] = g_prior[i];
-    if (tid < 12) S.uniform[tid] = g_uniform[tid];
+    for (int i = tid; i < 30 * 12; i += OBS_THREADS) S.bel_tab[i] = g_prior[i];
+    if (tid < 12) S.bel_tab[30 * 12 + tid] = g_uniform[tid];
     if (tid < 30) S.slot_ch[tid] = g_topo.slot_ch[tid];
     for (int i = tid; i < 2 * OBS_WORDS4; i += OBS_THREADS)
         reinterpret_cast<uint4 *>(S.buf[i / OBS_WORDS4].bits)[i % OBS_WORDS4] = make_uint4(0u, 0u, 0u, 0u);
@@ -567,7 +575,7 @@ __global__ void __launch_bounds__(OBS_THREADS, OBS_MIN_CTAS) obs_kernel(jq_batch
             UnitBuf &B = S.buf[bi];
             if (B.u < 0) break;
             if (k == 0 && tid == 0) JQ_TRACE_AT(0, TO_FIRST_STREAM);
-            stream_unit(B, S.prior, S.uniform, ext_bel != nullptr, spatial, global, warp, lane, OBS_STREAM_WARPS,
+            stream_unit(B, S.bel_tab, ext_bel != nullptr, spatial, global, warp, lane, OBS_STREAM_WARPS,
                         BAR_STREAM);
             if (tid == 0) JQ_TRACE_AT(0, TO_LAST_STREAMED);
             bar_arrive(BAR_EMPTY0 + bi, OBS_THREADS);  // buffer bi free again
