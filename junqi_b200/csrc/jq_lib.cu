@@ -356,7 +356,7 @@ int jq_init(int device) {
     CU(cudaMemcpyToSymbol(g_topo, &host_topo, sizeof(Topo)));
     CU(cudaMemcpyToSymbol(g_slot, &host_slot, sizeof(SlotTopo)));
     {
-        static uint32_t statw[4][4][STAT_WORDS];
+        static uint32_t statw[4][OBS_VEC][STAT_WORDS];
         build_static_words(host_topo, statw);
         CU(cudaMemcpyToSymbol(g_statw, statw, sizeof(statw)));
     }

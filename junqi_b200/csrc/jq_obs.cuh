@@ -8,10 +8,11 @@
 // other floats need: one record per piece (cell, belief code, direct-combat
 // pid set, recency values), the two progress constants, and an exception
 // list (float index, value) for the -1 of each history source.  The stream
-// starts 4 - head bits in, where head (0..3) is the number of floats before
-// the unit's first 16-byte boundary in global memory (a unit is 91,613
-// floats, so its base is only 4-byte aligned); every aligned float4 of the
-// output then owns one 4-bit nibble of a 32-bit word.
+// starts 8 - head bits in, where head (0..7) is the number of floats before
+// the unit's first 32-byte boundary in global memory (a unit is 91,613
+// floats, so its base is only 4-byte aligned); every aligned group of 8
+// floats of the output then owns one byte of a 32-bit word and is written
+// with one 32-byte store.
 //
 // Persistent CTAs of 16 warps, specialised:
 //  * 8 staging warps take units in memory order through an atomic ticket
@@ -54,21 +55,22 @@ static_assert(OBS_STAGE_WARPS % 4 == 0, "staging warps come in groups of four se
 constexpr int OBS_THREADS = 32 * (OBS_STREAM_WARPS + OBS_STAGE_WARPS);      // 384
 constexpr int OBS_WORDS = (OBS_FLOATS + 8 + 31) / 32;  // 2,864 words per stream
 constexpr int OBS_WORDS4 = (OBS_WORDS + 3) / 4;         // in uint4
-// The board-static planes 58-62 as stream words: they start in word
-// STAT_W0 for every stream offset 1..4 and span STAT_WORDS words.
-constexpr int STAT_W0 = (58 * NC + 1) >> 5, STAT_WORDS = ((63 * NC + 4) >> 5) - STAT_W0 + 1;
-static_assert(((58 * NC + 4) >> 5) == STAT_W0, "static planes start in one word for every offset");
+// Floats per vector store of the stream: the stream offset of a unit is 1..OBS_VEC.
+constexpr int OBS_VEC = 8;
+// The board-static planes 58-62 as stream words: for every stream offset
+// 1..OBS_VEC they lie within the STAT_WORDS words from STAT_W0.
+constexpr int STAT_W0 = (58 * NC + 1) >> 5, STAT_WORDS = ((63 * NC + OBS_VEC) >> 5) - STAT_W0 + 1;
 
 // Built on the host once (build_static_words), copied into each CTA.
-__device__ uint32_t g_statw[4][4][STAT_WORDS];
+__device__ uint32_t g_statw[4][OBS_VEC][STAT_WORDS];
 
 // The board-static bits (camp, stronghold, rail, nine-grid, arc planes
 // 58-62; observation.py:343-383) for observer o and stream offset s + 1,
 // as stream words from STAT_W0.
-inline void build_static_words(const Topo &T, uint32_t out[4][4][STAT_WORDS]) {
+inline void build_static_words(const Topo &T, uint32_t out[4][OBS_VEC][STAT_WORDS]) {
     const uint8_t fb[5] = {F_CAMP, F_SH, F_RAIL, F_NINE, F_ARC};
     for (int o = 0; o < 4; ++o)
-        for (int sh = 0; sh < 4; ++sh) {
+        for (int sh = 0; sh < OBS_VEC; ++sh) {
             for (int w = 0; w < STAT_WORDS; ++w) out[o][sh][w] = 0u;
             for (int f = 0; f < NC; ++f) {
                 const int cc = T.f2c[f];
@@ -122,7 +124,7 @@ struct __align__(16) UnitBuf {
 struct __align__(16) ObsSmem {
     UnitBuf buf[2];
     int16_t rotf[4][NC];                // world flat -> canonical flat, per observer seat
-    uint32_t statw[4][4][STAT_WORDS];   // board-static bits as stream words, per observer and stream offset
+    uint32_t statw[4][OBS_VEC][STAT_WORDS];  // board-static bits as stream words, per observer and stream offset
     int ticket[1], next_o[1];  // the staging warps' next unit and its observer
     // belief values: rows 0..29 the prior of a seat-local slot, row 30 the
     // uniform fallback (global loads here would wait behind the write stream)
@@ -146,7 +148,7 @@ __device__ __forceinline__ bool in_back_two(int seat, int zx, int zy) {
 __device__ __forceinline__ void set_bit(uint32_t *s, int q) { atomicOr(&s[q >> 5], 1u << (q & 31)); }
 
 // Writes one unit's bitstream and exception list; stream position of float
-// (ch, cell) is its output index ch * 289 + cell shifted by qoff = 4 - head.
+// (ch, cell) is its output index ch * 289 + cell shifted by qoff = OBS_VEC - head.
 struct Stager {
     UnitBuf &B;
     int qoff;
@@ -361,7 +363,17 @@ __device__ __forceinline__ float bit_value(const UnitBuf &B, int j, int qoff) {
 
 __device__ __forceinline__ int unit_head(const float *spatial, int u) {
     const float *out = spatial + (size_t)u * OBS_FLOATS;
-    return (int)((4 - (((uintptr_t)out >> 2) & 3)) & 3);
+    return (int)((OBS_VEC - (((uintptr_t)out >> 2) & (OBS_VEC - 1))) & (OBS_VEC - 1));
+}
+
+// Eight floats, bit i of `by` -> 1.0 else 0.0, as one 32-byte store (p is
+// 32-byte aligned).
+__device__ __forceinline__ void st_bits8(float *p, uint32_t by) {
+    asm volatile("st.global.v8.f32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p),
+                 "f"((by & 1u) ? 1.f : 0.f), "f"((by & 2u) ? 1.f : 0.f), "f"((by & 4u) ? 1.f : 0.f),
+                 "f"((by & 8u) ? 1.f : 0.f), "f"((by & 16u) ? 1.f : 0.f), "f"((by & 32u) ? 1.f : 0.f),
+                 "f"((by & 64u) ? 1.f : 0.f), "f"((by & 128u) ? 1.f : 0.f)
+                 : "memory");
 }
 
 // Staging warps: build unit u (observer o of env e) into B.  t = thread in 0..127.
@@ -375,7 +387,7 @@ __device__ void stage_unit(const jq_batch &b, int seats, int mode, const float *
     const int e = u / seats;
     const int tm = (o + 2) & 3, left = (o + 1) & 3, right = (o + 3) & 3;
     // B.bits arrive zeroed by the streaming warps
-    Stager st{B, 4 - head, S.rotf[o], ext_bel ? ext_bel + ((size_t)e * 4 + o) * 12 * NC : nullptr};
+    Stager st{B, OBS_VEC - head, S.rotf[o], ext_bel ? ext_bel + ((size_t)e * 4 + o) * 12 * NC : nullptr};
     if (t < 32) {  // observer-own pids per tracked type: one load per lane, one ballot per type
         const int ti = t < 30 ? tracked_idx(b.piece_type[PI(e, o * 30 + t)]) : -1;
         const int pos = o * 30;
@@ -477,24 +489,31 @@ __device__ void stream_unit(UnitBuf &B, const float *bel_tab, bool ext, float *s
                             float *global, int w, int lane, int nwarps, int bar_stream) {
     const int u = B.u, t = w * 32 + lane;
     float *out = spatial + (size_t)u * OBS_FLOATS;
-    const int head = unit_head(spatial, u), qoff = 4 - head;
-    const int body4 = (OBS_FLOATS - head) >> 2;
+    const int head = unit_head(spatial, u), qoff = OBS_VEC - head;
+    const int body8 = (OBS_FLOATS - head) >> 3;
     // pass 1: every float as 0 / 1 -- the head and tail floats one by one, the
-    // aligned body as float4 (warp w: one contiguous slab), branch-free
+    // aligned body in groups of 8 (warp w: one contiguous slab), branch-free
     if (t < head) out[t] = bit_value(B, t, qoff);
-    if (t >= 32 && t < 36) {
-        const int j = head + body4 * 4 + (t - 32);
+    if (t >= 32 && t < 32 + OBS_VEC) {
+        const int j = head + body8 * 8 + (t - 32);
         if (j < OBS_FLOATS) out[j] = bit_value(B, j, qoff);
     }
-    float4 *out4 = reinterpret_cast<float4 *>(out + head);
-    const int per = (body4 + nwarps - 1) / nwarps;
-    const int g0 = w * per, g1 = g0 + per < body4 ? g0 + per : body4;
-#pragma unroll 4
-    for (int g = g0 + lane; g < g1; g += 32) {
-        // float4 g holds output floats head + 4g .. +3 = stream bits 4g + 4 .. 4g + 7
-        const uint32_t nib = (B.bits[(g + 1) >> 3] >> (((g + 1) & 7) << 2)) & 15u;
-        out4[g] = make_float4((nib & 1u) ? 1.f : 0.f, (nib & 2u) ? 1.f : 0.f, (nib & 4u) ? 1.f : 0.f,
-                              (nib & 8u) ? 1.f : 0.f);
+    float *out8 = out + head;
+    const int per = (body8 + nwarps - 1) / nwarps;
+    const int g0 = w * per, g1 = g0 + per < body8 ? g0 + per : body8;
+    // group g holds output floats head + 8g .. +7 = stream bits 8g + 8 .. 8g
+    // + 15, byte g + 1 of the stream; four groups per lane and pass, their
+    // bytes loaded before the stores
+    for (int g = g0 + lane; g < g1; g += 128) {
+        uint32_t by[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int gi = g + 32 * i;
+            by[i] = gi < g1 ? (B.bits[(gi + 1) >> 2] >> (((gi + 1) & 3) << 3)) & 0xffu : 0u;
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            if (g + 32 * i < g1) st_bits8(out8 + 8 * (g + 32 * i), by[i]);
     }
     // pass 2, ordered after pass 1 by the streaming warps' barrier: the
     // floats that are neither 0 nor 1, over lines still in L2 -- exceptions,
@@ -561,7 +580,7 @@ __global__ void __launch_bounds__(OBS_THREADS, OBS_MIN_CTAS) obs_kernel(jq_batch
     if (tid < 30) S.slot_ch[tid] = g_topo.slot_ch[tid];
     for (int i = tid; i < 2 * OBS_WORDS4; i += OBS_THREADS)
         reinterpret_cast<uint4 *>(S.buf[i / OBS_WORDS4].bits)[i % OBS_WORDS4] = make_uint4(0u, 0u, 0u, 0u);
-    for (int i = tid; i < 16 * STAT_WORDS; i += OBS_THREADS) (&S.statw[0][0][0])[i] = (&g_statw[0][0][0])[i];
+    for (int i = tid; i < 4 * OBS_VEC * STAT_WORDS; i += OBS_THREADS) (&S.statw[0][0][0])[i] = (&g_statw[0][0][0])[i];
     // launched as a programmatic dependent (see the rules kernel): caller
     // memory -- tickets, state, outputs -- only after the previous kernel
     asm volatile("griddepcontrol.wait;" ::: "memory");
