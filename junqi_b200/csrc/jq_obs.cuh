@@ -591,11 +591,13 @@ __global__ void __launch_bounds__(OBS_THREADS, OBS_MIN_CTAS) obs_kernel(jq_batch
         for (int k = 0;; ++k) {
             const int bi = k & 1;
             bar_sync(BAR_FULL0 + bi, OBS_THREADS);  // buffer bi staged
+            if (tid == 0 && k < 3) JQ_TRACE_AT(0, TO_UNIT_STREAM0 + 2 * k);
             UnitBuf &B = S.buf[bi];
             if (B.u < 0) break;
             if (k == 0 && tid == 0) JQ_TRACE_AT(0, TO_FIRST_STREAM);
             stream_unit(B, S.bel_tab, ext_bel != nullptr, spatial, global, warp, lane, OBS_STREAM_WARPS,
                         BAR_STREAM);
+            if (tid == 0 && k < 3) JQ_TRACE_AT(0, TO_UNIT_STREAM0 + 2 * k + 1);
             if (tid == 0) JQ_TRACE_AT(0, TO_LAST_STREAMED);
             bar_arrive(BAR_EMPTY0 + bi, OBS_THREADS);  // buffer bi free again
         }
@@ -618,6 +620,7 @@ __global__ void __launch_bounds__(OBS_THREADS, OBS_MIN_CTAS) obs_kernel(jq_batch
             const int bi = k & 1;
             UnitBuf &B = S.buf[bi];
             if (k >= 2) bar_sync(BAR_EMPTY0 + bi, OBS_THREADS);  // unit k - 2 streamed out of buffer bi
+            if (t == 0 && (k == 2 || k == 3)) JQ_TRACE_AT(0, TO_UNIT_STAGE_START2 + k - 2);
             if (u >= units) {
                 if (t == 0) B.u = -1;
                 bar_arrive(BAR_FULL0 + bi, OBS_THREADS);
@@ -627,6 +630,7 @@ __global__ void __launch_bounds__(OBS_THREADS, OBS_MIN_CTAS) obs_kernel(jq_batch
             bar_sync(BAR_STAGE, OBS_STAGE_THREADS);    // unit staged by every staging thread
             if (k == 0 && t == 0) JQ_TRACE_AT(0, TO_FIRST_STAGED);
             if (t == 0) JQ_TRACE_AT(0, TO_LAST_STAGED);
+            if (t == 0 && k < 3) JQ_TRACE_AT(0, TO_UNIT_STAGED0 + k);
             bar_arrive(BAR_FULL0 + bi, OBS_THREADS);  // hand it to the streaming warps
             if (t == 0) {
                 const int un = atomicAdd(&ticket[0], 1);

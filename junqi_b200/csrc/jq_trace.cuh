@@ -18,7 +18,11 @@ constexpr int TRACE_POINTS = 20;
 
 // obs_kernel points
 enum : int { TO_ENTRY = 0, TO_WAITED = 1, TO_FIRST_STAGED = 2, TO_FIRST_STREAM = 3, TO_LAST_STREAMED = 4,
-             TO_EXIT = 5, TO_UNITS = 6, TO_LAST_TICKET = 7, TO_LAST_STAGED = 8 };
+             TO_EXIT = 5, TO_UNITS = 6, TO_LAST_TICKET = 7, TO_LAST_STAGED = 8,
+             // the CTA's units 0..2: streaming warp 0 passed the staged-buffer barrier (9 + 2k) and
+             // finished streaming (10 + 2k); staging finished (15 + k); staging of units 2, 3 began
+             // after the free-buffer barrier (18, 19)
+             TO_UNIT_STREAM0 = 9, TO_UNIT_STAGED0 = 15, TO_UNIT_STAGE_START2 = 18 };
 // rules_kernel points (the phases of warp 0's first env, then the CTA's exit)
 enum : int { TR_ENTRY = 0, TR_WAITED = 1, TR_LOADED = 2, TR_STEPPED = 3, TR_RESET = 4, TR_IDS = 5, TR_MASKED = 6,
              TR_EXIT = 7,

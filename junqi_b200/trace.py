@@ -52,9 +52,23 @@ def obs_timeline(t: np.ndarray) -> dict:
             "last_streamed_us_median": float(np.median(us(t[:, 4]))),
             "exit_us_min": float(us(t[:, 5]).min()), "exit_us_max": float(us(t[:, 5]).max()),
             "units_per_cta_min": int(t[:, 6].min()), "units_per_cta_max": int(t[:, 6].max()),
+            # units 1 and 2 of every CTA (us, median over CTAs and the two units): streaming warp 0
+            # waiting for the staged buffer, streaming; staging one unit (start to staged)
+            "steady_unit_us": _steady(t),
             # the tail: exits after the last ticket was taken (T0), split by whether the CTA
             # still had a staged unit waiting behind the one it was streaming at T0
             "tail_after_last_ticket_us": _tail(t)}
+
+
+def _steady(t: np.ndarray) -> dict:
+    """Per-unit phases of the CTAs' units 1 and 2 from the raw stamps."""
+    ok = t[:, 6] >= 4
+    u = t[ok].astype(np.int64)
+    wait = np.concatenate([u[:, 11] - u[:, 10], u[:, 13] - u[:, 12]]) / 1e3
+    stream = np.concatenate([u[:, 12] - u[:, 11], u[:, 14] - u[:, 13]]) / 1e3
+    stage = (u[:, 17] - u[:, 18]) / 1e3  # unit 2: began after its free-buffer barrier, staged
+    return {"stream_wait": round(float(np.median(wait)), 2), "stream": round(float(np.median(stream)), 2),
+            "stage_unit2": round(float(np.median(stage)), 2), "ctas": int(ok.sum())}
 
 
 def _tail(t: np.ndarray) -> dict:
