@@ -121,8 +121,8 @@ def rules_timeline(t: np.ndarray) -> dict:
     eng = np.array([s["engineer_max"] for s in shape])
     out["legal_dsts_by_shape"] = {
         "total_moves_p50_max": [int(np.median(tot)), int(tot.max())],
-        "corr_dsts_total": round(float(np.corrcoef(dst, tot)[0, 1]), 2) if tot.std() > 0 else None,
-        "corr_dsts_engineer_max": round(float(np.corrcoef(dst, eng)[0, 1]), 2) if eng.std() > 0 else None,
+        "corr_dsts_total": _corr(dst, tot),
+        "corr_dsts_engineer_max": _corr(dst, eng),
         "dsts_us_p50_by_total_quartile": [round(float(np.median(dst[(tot >= a) & (tot <= b)])), 2)
                                           for a, b in zip(np.percentile(tot, [0, 25, 50, 75]),
                                                           np.percentile(tot, [25, 50, 75, 100]))],
@@ -142,6 +142,13 @@ def rules_timeline(t: np.ndarray) -> dict:
                          "scalar_us_without_p50_max": [round(float(np.median(scal[~ran])), 2),
                                                        round(float(scal[~ran].max()), 2)]}
     return out
+
+
+def _corr(a: np.ndarray, b: np.ndarray):
+    """Pearson correlation rounded to 0.01, None when either side is constant."""
+    if a.std() == 0 or b.std() == 0:
+        return None
+    return round(float(np.corrcoef(a, b)[0, 1]), 2)
 
 
 def _legal_shape(v) -> dict:
