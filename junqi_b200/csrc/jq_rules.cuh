@@ -317,13 +317,17 @@ __device__ bool warp_has_moves(const TopoCore &T, const WEnv &w, int lane, int s
 // 4 mask bits -> 4 bytes of 0/1 (bit i -> byte i).
 __device__ __forceinline__ uint32_t nibble_bytes(uint32_t nib) { return (nib * 0x00204081u) & 0x01010101u; }
 
-// Mask bytes j0 .. j0 + 15 from the bitstream.
-__device__ __forceinline__ uint4 mask_chunk(const WEnv &w, int j0) {
+// Mask bytes j0 .. j0 + 31 from the bitstream as one 32-byte store (p is
+// 32-byte aligned).
+__device__ __forceinline__ void mask_store32(uint8_t *p, const WEnv &w, int j0) {
     const int wi = j0 >> 5;
-    const uint32_t bits = __funnelshift_r(w.cbits[wi], w.cbits[wi + 1], j0 & 31) & 0xffffu;
-    if (!bits) return make_uint4(0u, 0u, 0u, 0u);
-    return make_uint4(nibble_bytes(bits & 15u), nibble_bytes((bits >> 4) & 15u), nibble_bytes((bits >> 8) & 15u),
-                      nibble_bytes(bits >> 12));
+    const uint32_t bits = __funnelshift_r(w.cbits[wi], w.cbits[wi + 1], j0 & 31);
+    uint32_t v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = nibble_bytes((bits >> (4 * i)) & 15u);
+    asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(v[0]), "r"(v[1]),
+                 "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+                 : "memory");
 }
 
 // Legal actions of `seat` (empty when `skip`), ascending, written to ids
@@ -405,12 +409,12 @@ __device__ int warp_legal(const TopoCore &T, WEnv &w, int lane, int seat, bool s
             }
         }
         __syncwarp();
-        const int head = (int)((16 - ((uintptr_t)mask_env & 15)) & 15);
+        // 32-byte stores from the first 32-byte boundary of the row
+        const int head = (int)((32 - ((uintptr_t)mask_env & 31)) & 31);
         for (int j = lane; j < head; j += 32) mask_env[j] = (uint8_t)((w.cbits[j >> 5] >> (j & 31)) & 1u);
-        const int body = (MASK_BYTES - head) >> 4;
-        for (int k = lane; k < body; k += 32)
-            *reinterpret_cast<uint4 *>(mask_env + head + k * 16) = mask_chunk(w, head + k * 16);
-        for (int j = head + body * 16 + lane; j < MASK_BYTES; j += 32)
+        const int body = (MASK_BYTES - head) >> 5;
+        for (int k = lane; k < body; k += 32) mask_store32(mask_env + head + k * 32, w, head + k * 32);
+        for (int j = head + body * 32 + lane; j < MASK_BYTES; j += 32)
             mask_env[j] = (uint8_t)((w.cbits[j >> 5] >> (j & 31)) & 1u);
         __syncwarp();
     }
